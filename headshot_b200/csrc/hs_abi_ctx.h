@@ -1,0 +1,31 @@
+// hs_abi_ctx.h — the opaque hs_ctx behind include/headshot_cuda.h.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <atomic>
+#include <string>
+
+#include "../../include/headshot_cuda.h"
+
+struct hs_ctx {
+  int device = 0;
+  int sm_count = 0;
+  cudaStream_t stream = nullptr;       // owned
+  cudaStream_t user_stream = nullptr;  // borrowed (hs_ctx_set_stream); may be the legacy stream 0
+  bool has_user_stream = false;
+  int* d_status = nullptr;             // device status word: first bounded-wait site that timed out
+  void* scratch = nullptr;             // normalised/rotated K (and 16-bit V for f32 callers)
+  size_t scratch_bytes = 0;
+  uint32_t wait_timeout_ms = 2000;
+  std::atomic<int> cancel{0};
+};
+
+namespace hs {
+hs_status abi_fail(hs_status s, const std::string& msg);
+hs_status abi_cuda_fail(cudaError_t e, const char* what);
+cudaStream_t ctx_stream(hs_ctx* ctx);
+uint64_t ctx_timeout_ns(hs_ctx* ctx);
+hs_status ctx_scratch(hs_ctx* ctx, size_t bytes, void** out);
+}  // namespace hs

@@ -1,0 +1,66 @@
+// hs_internal.h — launchers shared between the kernel files and the C ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+namespace hs {
+
+// Storage element codes used inside the library (match hs_dtype).
+enum ElemCode : int { kF32 = 0, kF16 = 1, kBF16 = 2 };
+
+inline size_t elem_bytes(int code) { return code == kF32 ? 4 : 2; }
+
+// QK-norm + 2D RoPE applied to a head vector (D = 64) in f32, in the order
+// of the reference block (LayerNorm, then rotate-half RoPE).
+struct QkPrologue {
+  const float* ln_w = nullptr;  // (64) f32, used when ln != 0
+  const float* ln_b = nullptr;  // (64) f32
+  float eps = 1e-5f;
+  int ln = 0;
+  const float* sin_t = nullptr;  // (P, 64) f32, used when rope != 0
+  const float* cos_t = nullptr;
+  uint32_t prefix = 0;            // tokens [0, prefix) of every frame pass through
+  uint32_t tokens_per_frame = 0;  // table row of token t is (t mod tpf) - prefix
+  int rope = 0;
+  uint32_t pos_offset = 0;  // global index of this shard's token 0 (ring shards)
+};
+
+// Running softmax state for attention split over several launches (ring
+// steps): per query row the unnormalised f32 accumulator O (64), the running
+// max m (log2 domain, scaled) and the running sum l.
+struct AttnState {
+  float* o = nullptr;  // (SH, T, 64) f32
+  float* m = nullptr;  // (SH, T) f32
+  float* l = nullptr;  // (SH, T) f32
+  int load = 0;        // read the state before the first KV tile
+  int store = 0;       // write the state instead of the normalised output
+};
+
+// Fused flash attention on tcgen05 (D = 64).  Keys/values are 16-bit
+// (`elem` = kF16 or kBF16); q may be 16-bit of the same type or f32;
+// out is written in `out_code` (kF32 or `elem`).  The Q tile receives the
+// QK-norm/RoPE prologue in-kernel; K must already be normalised/rotated.
+cudaError_t launch_attention_sm100(cudaStream_t stream, int elem, const void* q, int q_code, const void* k,
+                                   const void* v, void* out, int out_code, uint32_t sh, uint32_t t_q,
+                                   uint32_t t_kv, float scale, const QkPrologue& qp, const AttnState& st,
+                                   int* status, uint64_t timeout_ns, std::string* err);
+
+// Row prep for K (and for casts): out = RoPE(LN(x)) in `out_code` storage.
+cudaError_t launch_qk_prep(cudaStream_t stream, const void* x, int in_code, void* out, int out_code,
+                           uint64_t rows, uint32_t t, const QkPrologue& p);
+
+// Companion ops of the reference engine.
+cudaError_t launch_layernorm(cudaStream_t stream, const void* x, void* out, int code, const float* w,
+                             const float* b, uint64_t rows, uint32_t dim, float eps);
+cudaError_t launch_rope_apply(cudaStream_t stream, void* x, int code, const float* sin_t, const float* cos_t,
+                              uint32_t s, uint32_t h, uint32_t t, uint32_t d, uint32_t prefix,
+                              uint32_t tokens_per_frame);
+cudaError_t launch_split_heads(cudaStream_t stream, const void* x, void* out, int code, uint32_t s, uint32_t t,
+                               uint32_t h, uint32_t d);
+cudaError_t launch_attn_merge(cudaStream_t stream, const void* x, void* out, int code, uint32_t s, uint32_t h,
+                              uint32_t t, uint32_t d);
+
+}  // namespace hs

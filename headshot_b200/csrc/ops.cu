@@ -1,0 +1,302 @@
+// ops.cu — memory-bound companions of the attention op:
+//   qk_prep      K' = RoPE(LN(K)) (and plain 16-bit casts), one pass over HBM
+//   layernorm    GpuContext::layernorm  (src/engine/ops.rs:130-153, shaders/layernorm.wesl)
+//   rope_apply   GpuContext::rope_apply (src/engine/ops.rs:202-223, shaders/rope_apply.wesl)
+//   split_heads  GpuContext::split_heads (src/engine/ops.rs:185-200, shaders/split_heads.wesl)
+//   attn_merge   GpuContext::attn_merge  (src/engine/ops.rs:255-267, shaders/attn_merge.wesl)
+// Storage may be f32, f16 or bf16; all arithmetic is f32.
+#include "hs_internal.h"
+#include "hs_ptx.cuh"
+
+namespace hs {
+namespace {
+
+template <typename T>
+__device__ __forceinline__ float ld_f(const T* p);
+template <>
+__device__ __forceinline__ float ld_f<float>(const float* p) { return *p; }
+template <>
+__device__ __forceinline__ float ld_f<__half>(const __half* p) { return __half2float(*p); }
+template <>
+__device__ __forceinline__ float ld_f<__nv_bfloat16>(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+
+template <typename T>
+__device__ __forceinline__ T cvt_to(float f);
+template <>
+__device__ __forceinline__ float cvt_to<float>(float f) { return f; }
+template <>
+__device__ __forceinline__ __half cvt_to<__half>(float f) { return __float2half_rn(f); }
+template <>
+__device__ __forceinline__ __nv_bfloat16 cvt_to<__nv_bfloat16>(float f) { return __float2bfloat16_rn(f); }
+
+// Eight consecutive elements <-> f32.
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float (&v)[8]) {
+  if constexpr (sizeof(T) == 4) {
+    const float4 a = reinterpret_cast<const float4*>(p)[0];
+    const float4 b = reinterpret_cast<const float4*>(p)[1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = Elem<T>::unpack2(w[i]);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void store8(T* p, const float (&v)[8]) {
+  if constexpr (sizeof(T) == 4) {
+    reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+    reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+  } else {
+    uint4 u;
+    u.x = Elem<T>::pack2(v[0], v[1]);
+    u.y = Elem<T>::pack2(v[2], v[3]);
+    u.z = Elem<T>::pack2(v[4], v[5]);
+    u.w = Elem<T>::pack2(v[6], v[7]);
+    *reinterpret_cast<uint4*>(p) = u;
+  }
+}
+
+// Eight threads per 64-wide row; thread g holds elements [8g, 8g+8).  The
+// RoPE partner of element i < 32 is i + 32, held by thread g ^ 4.
+template <typename In, typename Out>
+__global__ void __launch_bounds__(256) qk_prep_kernel(const In* __restrict__ x, Out* __restrict__ out, uint64_t rows,
+                                                      uint32_t t, QkPrologue p) {
+  const uint64_t gt = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const uint64_t row = gt >> 3;
+  const int g = static_cast<int>(gt & 7);
+  const bool valid = row < rows;
+  float v[8];
+  if (valid) {
+    load8(x + row * 64 + 8 * g, v);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = 0.f;
+  }
+  if (p.ln) {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s += v[i];
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    s += __shfl_xor_sync(0xffffffffu, s, 4);
+    const float mu = s * (1.0f / 64);
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float d = v[i] - mu;
+      q = fmaf(d, d, q);
+    }
+    q += __shfl_xor_sync(0xffffffffu, q, 1);
+    q += __shfl_xor_sync(0xffffffffu, q, 2);
+    q += __shfl_xor_sync(0xffffffffu, q, 4);
+    const float inv = rsqrtf(q * (1.0f / 64) + p.eps);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = (v[i] - mu) * inv * __ldg(p.ln_w + 8 * g + i) + __ldg(p.ln_b + 8 * g + i);
+  }
+  if (p.rope) {
+    float pv[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) pv[i] = __shfl_xor_sync(0xffffffffu, v[i], 4);
+    const uint32_t tok = static_cast<uint32_t>(row % t);
+    const uint32_t ft = (tok + p.pos_offset) % p.tokens_per_frame;
+    if (valid && ft >= p.prefix) {
+      const uint64_t r = static_cast<uint64_t>(ft - p.prefix) * 64 + 8 * g;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float sn = __ldg(p.sin_t + r + i), cs = __ldg(p.cos_t + r + i);
+        // lower half: x*cos - x[i+32]*sin ; upper half: x*cos + x[i-32]*sin
+        v[i] = g < 4 ? v[i] * cs - pv[i] * sn : v[i] * cs + pv[i] * sn;
+      }
+    }
+  }
+  if (valid) store8(out + row * 64 + 8 * g, v);
+}
+
+// One warp per row, any width; two-pass statistics like layernorm.wesl.
+template <typename T>
+__global__ void __launch_bounds__(256) layernorm_kernel(const T* __restrict__ x, T* __restrict__ out,
+                                                        const float* __restrict__ w, const float* __restrict__ b,
+                                                        uint64_t rows, uint32_t dim, float eps) {
+  const uint64_t row = (static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const T* xr = x + row * dim;
+  float s = 0.f;
+  for (uint32_t j = lane; j < dim; j += 32) s += ld_f(xr + j);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const float mu = s / static_cast<float>(dim);
+  float q = 0.f;
+  for (uint32_t j = lane; j < dim; j += 32) {
+    const float d = ld_f(xr + j) - mu;
+    q = fmaf(d, d, q);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+  const float inv = rsqrtf(q / static_cast<float>(dim) + eps);
+  T* orow = out + row * dim;
+  for (uint32_t j = lane; j < dim; j += 32) orow[j] = cvt_to<T>((ld_f(xr + j) - mu) * inv * w[j] + b[j]);
+}
+
+// One thread per rotation pair, in place (rope_apply.wesl:36-56).
+template <typename T>
+__global__ void __launch_bounds__(256) rope_apply_kernel(T* __restrict__ x, const float* __restrict__ sin_t,
+                                                         const float* __restrict__ cos_t, uint32_t s, uint32_t h,
+                                                         uint32_t t, uint32_t d, uint32_t prefix, uint32_t tpf) {
+  const uint32_t half = d / 2;
+  const uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const uint64_t total = static_cast<uint64_t>(s) * h * t * half;
+  if (i >= total) return;
+  const uint32_t dp = static_cast<uint32_t>(i % half);
+  const uint64_t tok_flat = i / half;  // (s*h)*t + t
+  const uint32_t tok = static_cast<uint32_t>(tok_flat % t);
+  const uint32_t ft = tok % tpf;
+  if (ft < prefix) return;
+  const uint64_t row = static_cast<uint64_t>(ft - prefix) * d;
+  const uint64_t base = tok_flat * d + dp;
+  const float lo = ld_f(x + base), hi = ld_f(x + base + half);
+  x[base] = cvt_to<T>(lo * cos_t[row + dp] - hi * sin_t[row + dp]);
+  x[base + half] = cvt_to<T>(hi * cos_t[row + half + dp] + lo * sin_t[row + half + dp]);
+}
+
+// (S*T, H*D) <-> (S, H, T, D); `merge` selects the direction.  One thread
+// per 16-byte chunk when D allows it, else per element.
+template <typename T, int V>
+__global__ void __launch_bounds__(256) permute_heads_kernel(const T* __restrict__ x, T* __restrict__ out, uint32_t s,
+                                                            uint32_t h, uint32_t t, uint32_t d, int merge) {
+  const uint64_t i = (static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * V;
+  const uint64_t total = static_cast<uint64_t>(s) * h * t * d;
+  if (i >= total) return;
+  // head-major index decode (s, h, t, d)
+  const uint32_t dd = static_cast<uint32_t>(i % d);
+  const uint64_t r1 = i / d;
+  const uint32_t tt = static_cast<uint32_t>(r1 % t);
+  const uint64_t r2 = r1 / t;
+  const uint32_t hh = static_cast<uint32_t>(r2 % h);
+  const uint64_t ss = r2 / h;
+  const uint64_t tok = ((ss * t + tt) * h + hh) * d + dd;  // token-major index
+  const uint64_t src = merge ? i : tok;
+  const uint64_t dst = merge ? tok : i;
+  if constexpr (V * sizeof(T) == 16) {
+    *reinterpret_cast<uint4*>(out + dst) = *reinterpret_cast<const uint4*>(x + src);
+  } else {
+#pragma unroll
+    for (int k = 0; k < V; ++k) out[dst + k] = x[src + k];
+  }
+}
+
+inline unsigned blocks_for(uint64_t threads, unsigned per_block) {
+  return static_cast<unsigned>((threads + per_block - 1) / per_block);
+}
+
+template <typename In>
+cudaError_t prep_dispatch_out(cudaStream_t stream, const In* x, void* out, int out_code, uint64_t rows, uint32_t t,
+                              const QkPrologue& p) {
+  const unsigned grid = blocks_for(rows * 8, 256);
+  switch (out_code) {
+    case kBF16:
+      qk_prep_kernel<In, __nv_bfloat16><<<grid, 256, 0, stream>>>(x, static_cast<__nv_bfloat16*>(out), rows, t, p);
+      break;
+    case kF16:
+      qk_prep_kernel<In, __half><<<grid, 256, 0, stream>>>(x, static_cast<__half*>(out), rows, t, p);
+      break;
+    default:
+      qk_prep_kernel<In, float><<<grid, 256, 0, stream>>>(x, static_cast<float*>(out), rows, t, p);
+      break;
+  }
+  return cudaGetLastError();
+}
+
+template <template <typename> class F, typename... A>
+cudaError_t by_code(int code, A... args) {
+  switch (code) {
+    case kBF16: return F<__nv_bfloat16>::run(args...);
+    case kF16: return F<__half>::run(args...);
+    default: return F<float>::run(args...);
+  }
+}
+
+template <typename T>
+struct LayerNormRun {
+  static cudaError_t run(cudaStream_t st, const void* x, void* out, const float* w, const float* b, uint64_t rows,
+                         uint32_t dim, float eps) {
+    layernorm_kernel<T><<<blocks_for(rows * 32, 256), 256, 0, st>>>(static_cast<const T*>(x), static_cast<T*>(out), w,
+                                                                     b, rows, dim, eps);
+    return cudaGetLastError();
+  }
+};
+
+template <typename T>
+struct RopeRun {
+  static cudaError_t run(cudaStream_t st, void* x, const float* sn, const float* cs, uint32_t s, uint32_t h,
+                         uint32_t t, uint32_t d, uint32_t prefix, uint32_t tpf) {
+    const uint64_t total = static_cast<uint64_t>(s) * h * t * (d / 2);
+    rope_apply_kernel<T><<<blocks_for(total, 256), 256, 0, st>>>(static_cast<T*>(x), sn, cs, s, h, t, d, prefix, tpf);
+    return cudaGetLastError();
+  }
+};
+
+template <typename T>
+struct PermuteRun {
+  static cudaError_t run(cudaStream_t st, const void* x, void* out, uint32_t s, uint32_t h, uint32_t t, uint32_t d,
+                         int merge) {
+    const uint64_t total = static_cast<uint64_t>(s) * h * t * d;
+    constexpr int kVec = 16 / sizeof(T);
+    const bool vec = (d % kVec) == 0 && (reinterpret_cast<uintptr_t>(x) % 16) == 0 &&
+                     (reinterpret_cast<uintptr_t>(out) % 16) == 0;
+    if (vec)
+      permute_heads_kernel<T, kVec><<<blocks_for(total / kVec, 256), 256, 0, st>>>(
+          static_cast<const T*>(x), static_cast<T*>(out), s, h, t, d, merge);
+    else
+      permute_heads_kernel<T, 1><<<blocks_for(total, 256), 256, 0, st>>>(static_cast<const T*>(x),
+                                                                          static_cast<T*>(out), s, h, t, d, merge);
+    return cudaGetLastError();
+  }
+};
+
+}  // namespace
+
+cudaError_t launch_qk_prep(cudaStream_t stream, const void* x, int in_code, void* out, int out_code, uint64_t rows,
+                           uint32_t t, const QkPrologue& p) {
+  if (rows == 0) return cudaSuccess;
+  switch (in_code) {
+    case kBF16: return prep_dispatch_out(stream, static_cast<const __nv_bfloat16*>(x), out, out_code, rows, t, p);
+    case kF16: return prep_dispatch_out(stream, static_cast<const __half*>(x), out, out_code, rows, t, p);
+    default: return prep_dispatch_out(stream, static_cast<const float*>(x), out, out_code, rows, t, p);
+  }
+}
+
+cudaError_t launch_layernorm(cudaStream_t stream, const void* x, void* out, int code, const float* w, const float* b,
+                             uint64_t rows, uint32_t dim, float eps) {
+  if (rows == 0 || dim == 0) return cudaSuccess;
+  return by_code<LayerNormRun>(code, stream, x, out, w, b, rows, dim, eps);
+}
+
+cudaError_t launch_rope_apply(cudaStream_t stream, void* x, int code, const float* sin_t, const float* cos_t,
+                              uint32_t s, uint32_t h, uint32_t t, uint32_t d, uint32_t prefix,
+                              uint32_t tokens_per_frame) {
+  if (static_cast<uint64_t>(s) * h * t * d == 0) return cudaSuccess;
+  return by_code<RopeRun>(code, stream, x, sin_t, cos_t, s, h, t, d, prefix, tokens_per_frame);
+}
+
+cudaError_t launch_split_heads(cudaStream_t stream, const void* x, void* out, int code, uint32_t s, uint32_t t,
+                               uint32_t h, uint32_t d) {
+  if (static_cast<uint64_t>(s) * h * t * d == 0) return cudaSuccess;
+  return by_code<PermuteRun>(code, stream, x, out, s, h, t, d, 0);
+}
+
+cudaError_t launch_attn_merge(cudaStream_t stream, const void* x, void* out, int code, uint32_t s, uint32_t h,
+                              uint32_t t, uint32_t d) {
+  if (static_cast<uint64_t>(s) * h * t * d == 0) return cudaSuccess;
+  return by_code<PermuteRun>(code, stream, x, out, s, h, t, d, 1);
+}
+
+}  // namespace hs

@@ -1,0 +1,204 @@
+"""Host-side mirror of headshot-server's `GpuContext` attention ops.
+
+Same op names, argument meaning and layouts as
+crates/headshot-server/src/engine/ops.rs; tensors are torch CUDA tensors
+(PyTorch supplies device memory and the stream — the arithmetic runs in
+libheadshot_cuda.so through the C ABI).  Where the reference `assert!`s
+(shape, dtype, table size) this raises AssertionError before launching;
+errors reported by the library raise `HsError`.
+
+    ctx = GpuContext()
+    out = ctx.attention(q, k, v)                    # ops.rs:228-253
+    q = ctx.layernorm(q, w, b)                      # ops.rs:130-153 (eps 1e-5)
+    ctx.rope_apply(q, sin, cos, prefix)             # ops.rs:202-223, in place
+    heads = ctx.split_heads(x, s, t, h, d)          # ops.rs:185-200
+    merged = ctx.attn_merge(heads)                  # ops.rs:255-267
+    out = ctx.attention_fused(q, k, v, qk_norm=QkNorm(...), rope=Rope(...))
+                                                    # block.rs:136-148 as one op
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from ._lib import HsError, check  # noqa: F401  (re-exported)
+
+_DTYPES = {torch.float32: _lib.HS_F32, torch.float16: _lib.HS_F16, torch.bfloat16: _lib.HS_BF16}
+
+
+def _code(t: torch.Tensor) -> int:
+    assert t.dtype in _DTYPES, f"unsupported dtype {t.dtype}"
+    return _DTYPES[t.dtype]
+
+
+def _ptr(t: torch.Tensor | None):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+@dataclass
+class QkNorm:
+    """LayerNorm(64) weights for q and k (block.rs:35-40); f32 device tensors."""
+
+    q_w: torch.Tensor
+    q_b: torch.Tensor
+    k_w: torch.Tensor
+    k_b: torch.Tensor
+    eps: float = 1e-5
+
+
+@dataclass
+class Rope:
+    """RoPE tables + unrotated prefix (block.rs:42-47).  `tokens_per_frame`
+    extends the reference for sequences of several frames (global attention
+    with per-frame positions); None means the whole sequence is one frame."""
+
+    sin: torch.Tensor
+    cos: torch.Tensor
+    prefix: int
+    tokens_per_frame: int | None = None
+
+
+class GpuContext:
+    """One device + one stream, like engine::GpuContext (src/engine/mod.rs)."""
+
+    def __init__(self, device: int = 0):
+        self._L = _lib.lib()
+        h = ctypes.c_void_p()
+        check(self._L.hs_ctx_create(device, ctypes.byref(h)))
+        self._h = h
+        self.device = torch.device("cuda", device)
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            self._L.hs_ctx_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def handle(self) -> ctypes.c_void_p:
+        return self._h
+
+    def _bind_stream(self) -> None:
+        # Order our launches with torch's work on the same device.
+        check(self._L.hs_ctx_set_stream(self._h, ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)))
+
+    def _check_tensor(self, t: torch.Tensor, name: str) -> None:
+        assert t.is_cuda and t.device == self.device, f"{name} must live on {self.device}"
+        assert t.is_contiguous(), f"{name} must be contiguous"
+
+    # ------------------------------------------------------------ ops ----
+
+    def attention(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float | None = None) -> torch.Tensor:
+        """Non-causal attention over head-major (S, H, T, D); allocates `out` (ops.rs:228-253)."""
+        assert q.dim() == 4, "attention wants (S,H,T,D)"
+        assert q.shape == k.shape and q.shape == v.shape, "q/k/v shape mismatch"
+        assert q.dtype == k.dtype == v.dtype, "q/k/v dtype mismatch"
+        s, h, t, d = q.shape
+        assert s * h <= 65535, "attention grid y overflow"
+        for n, x in (("q", q), ("k", k), ("v", v)):
+            self._check_tensor(x, n)
+        out = torch.empty_like(q)
+        self._bind_stream()
+        check(self._L.hs_attention(self._h, _ptr(q), _ptr(k), _ptr(v), _ptr(out), s, h, t, d, _code(q),
+                                   0.0 if scale is None else float(scale)))
+        return out
+
+    def attention_fused(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, qk_norm: QkNorm | None = None,
+                        rope: Rope | None = None, scale: float | None = None,
+                        out: torch.Tensor | None = None) -> torch.Tensor:
+        """QK-norm -> RoPE -> attention (block.rs:136-148) in one call."""
+        assert q.dim() == 4, "attention wants (S,H,T,D)"
+        assert q.shape == k.shape and q.shape == v.shape, "q/k/v shape mismatch"
+        assert q.dtype == k.dtype == v.dtype, "q/k/v dtype mismatch"
+        s, h, t, d = q.shape
+        for n, x in (("q", q), ("k", k), ("v", v)):
+            self._check_tensor(x, n)
+        if out is None:
+            out = torch.empty_like(q)
+        assert out.shape == q.shape and out.dtype == q.dtype
+        n_args = [None] * 4
+        eps = 1e-5
+        if qk_norm is not None:
+            for x in (qk_norm.q_w, qk_norm.q_b, qk_norm.k_w, qk_norm.k_b):
+                assert x.dtype == torch.float32 and x.numel() == d, "norm weight must be f32 (D)"
+                self._check_tensor(x, "qk_norm")
+            n_args = [qk_norm.q_w, qk_norm.q_b, qk_norm.k_w, qk_norm.k_b]
+            eps = qk_norm.eps
+        r_sin = r_cos = None
+        rows = prefix = tpf = 0
+        if rope is not None:
+            assert rope.sin.dtype == torch.float32 and rope.cos.dtype == torch.float32, "rope tables must be f32"
+            assert rope.sin.shape == rope.cos.shape and rope.sin.shape[-1] == d, "table size"
+            self._check_tensor(rope.sin, "rope.sin")
+            self._check_tensor(rope.cos, "rope.cos")
+            r_sin, r_cos = rope.sin, rope.cos
+            rows = rope.sin.numel() // d
+            prefix = rope.prefix
+            tpf = rope.tokens_per_frame or t
+        self._bind_stream()
+        check(self._L.hs_attention_fused(
+            self._h, _ptr(q), _ptr(k), _ptr(v), _ptr(out), s, h, t, d, _code(q),
+            0.0 if scale is None else float(scale), *[_ptr(x) for x in n_args], float(eps), _ptr(r_sin), _ptr(r_cos),
+            rows, prefix, tpf))
+        return out
+
+    def layernorm(self, x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:
+        """Row LayerNorm over the last dim, f32 statistics (ops.rs:130-153; the reference fixes eps 1e-5)."""
+        dim = x.shape[-1]
+        rows = x.numel() // dim
+        assert weight.numel() == dim and bias.numel() == dim
+        assert weight.dtype == torch.float32, "norm weight must be f32"
+        assert bias.dtype == torch.float32, "norm bias must be f32"
+        for n, t in (("x", x), ("weight", weight), ("bias", bias)):
+            self._check_tensor(t, n)
+        out = torch.empty_like(x)
+        self._bind_stream()
+        check(self._L.hs_layernorm(self._h, _ptr(x), _ptr(weight), _ptr(bias), _ptr(out), rows, dim, float(eps),
+                                   _code(x)))
+        return out
+
+    def rope_apply(self, x: torch.Tensor, sin: torch.Tensor, cos: torch.Tensor, prefix: int) -> None:
+        """In-place RoPE on (S,H,T,D); tables (T - prefix, D) f32 (ops.rs:202-223)."""
+        assert x.dim() == 4, "rope_apply wants (S,H,T,D)"
+        s, h, t, d = x.shape
+        assert sin.numel() == (t - prefix) * d, "table size"
+        assert sin.dtype == torch.float32 and cos.dtype == torch.float32, "rope tables must be f32"
+        for n, tt in (("x", x), ("sin", sin), ("cos", cos)):
+            self._check_tensor(tt, n)
+        self._bind_stream()
+        check(self._L.hs_rope_apply(self._h, _ptr(x), _ptr(sin), _ptr(cos), t - prefix, s, h, t, d, prefix, _code(x)))
+
+    def split_heads(self, x: torch.Tensor, s: int, t: int, h: int, d: int) -> torch.Tensor:
+        """(S*T, H*D) -> head-major (S, H, T, D) (ops.rs:185-200)."""
+        assert x.numel() == s * t * h * d
+        self._check_tensor(x, "x")
+        out = torch.empty((s, h, t, d), dtype=x.dtype, device=x.device)
+        self._bind_stream()
+        check(self._L.hs_split_heads(self._h, _ptr(x), _ptr(out), s, t, h, d, _code(x)))
+        return out
+
+    def attn_merge(self, x: torch.Tensor) -> torch.Tensor:
+        """(S, H, T, D) -> (S*T, H*D) (ops.rs:255-267)."""
+        assert x.dim() == 4, "attn_merge wants (S,H,T,D)"
+        s, h, t, d = x.shape
+        self._check_tensor(x, "x")
+        out = torch.empty((s * t, h * d), dtype=x.dtype, device=x.device)
+        self._bind_stream()
+        check(self._L.hs_attn_merge(self._h, _ptr(x), _ptr(out), s, h, t, d, _code(x)))
+        return out
+
+    def sync(self) -> None:
+        """Wait for the stream; raises HsError(HS_ERR_TIMEOUT) if an in-kernel wait gave up."""
+        self._bind_stream()
+        check(self._L.hs_sync(self._h))
+
+    def set_wait_timeout_ms(self, ms: int) -> None:
+        check(self._L.hs_ctx_set_wait_timeout_ms(self._h, int(ms)))

@@ -1,0 +1,154 @@
+/*
+ * headshot_cuda.h — C ABI of the B200 (sm_100a) attention path for
+ * headshot-server's aggregator.
+ *
+ * Drop-in boundary: each entry point replaces one `GpuContext` op of the
+ * reference engine (Feilkin/headshot, crates/headshot-server/src/engine/),
+ * keeping its tensor layouts and argument meaning.  Plain pointers and sizes
+ * only; device pointers come from hs_alloc (or any CUDA allocation on the
+ * context's device).  Every call is asynchronous on the context's stream;
+ * hs_sync waits and reports deferred device errors, like the reference's
+ * flush/download (src/engine/mod.rs:261-284).
+ *
+ * Errors: where the reference panics through assert! (shape, dtype, table
+ * size), these functions return HS_ERR_INVALID and leave a message for
+ * hs_last_error(); they never abort or throw across the ABI.
+ *
+ * Layouts (as in the reference):
+ *   head-major  (S, H, T, D)  contiguous — attention q/k/v/out
+ *   token-major (S*T, H*D)    contiguous — GEMM activations
+ *   RoPE tables (P, 64) f32, P = patch rows
+ */
+#ifndef HEADSHOT_CUDA_H
+#define HEADSHOT_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define HS_ABI_VERSION 1u
+
+#if defined(__GNUC__)
+#define HS_API __attribute__((visibility("default")))
+#else
+#define HS_API
+#endif
+
+typedef enum hs_status {
+  HS_OK = 0,
+  HS_ERR_INVALID = 1,     /* contract violated; the reference would panic */
+  HS_ERR_UNSUPPORTED = 2, /* valid request this build does not implement */
+  HS_ERR_CUDA = 3,        /* CUDA runtime error */
+  HS_ERR_OOM = 4,         /* device allocation failed */
+  HS_ERR_TIMEOUT = 5,     /* a kernel's bounded wait gave up; context stays usable */
+  HS_ERR_NCCL = 6,        /* NCCL error in a multi-GPU call */
+  HS_ERR_CANCELLED = 7    /* cancellation requested (src/engine/mod.rs:102-106) */
+} hs_status;
+
+/* Storage types: the reference's Dtype::{F32,F16} (src/engine/tensor.rs:13-16) plus bf16. */
+typedef enum hs_dtype { HS_F32 = 0, HS_F16 = 1, HS_BF16 = 2 } hs_dtype;
+
+typedef struct hs_ctx hs_ctx;
+
+/* ------------------------------------------------------------ context --- */
+
+HS_API uint32_t hs_abi_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+HS_API const char* hs_last_error(void);
+
+/* Replaces GpuContext::new (src/engine/mod.rs:111-211): binds `device`,
+ * creates the context's stream and device status word. */
+HS_API hs_status hs_ctx_create(int device, hs_ctx** out);
+HS_API hs_status hs_ctx_destroy(hs_ctx* ctx);
+
+/* Run subsequent calls on a caller-owned cudaStream_t (NULL is the legacy
+ * default stream); hs_ctx_use_own_stream returns to the context's stream. */
+HS_API hs_status hs_ctx_set_stream(hs_ctx* ctx, void* stream);
+HS_API hs_status hs_ctx_use_own_stream(hs_ctx* ctx);
+HS_API void* hs_ctx_stream(hs_ctx* ctx);
+
+/* Upper bound for every in-kernel wait, in milliseconds (default 2000). */
+HS_API hs_status hs_ctx_set_wait_timeout_ms(hs_ctx* ctx, uint32_t ms);
+
+/* Cooperative cancellation (src/engine/mod.rs:92-95, :286-304): multi-step
+ * calls check the flag between steps and return HS_ERR_CANCELLED. */
+HS_API hs_status hs_ctx_request_cancel(hs_ctx* ctx);
+HS_API hs_status hs_ctx_clear_cancel(hs_ctx* ctx);
+
+/* ------------------------------------------------------------- memory --- */
+
+/* Stream-ordered device pool; replaces GpuContext::empty_typed /
+ * create_buffer (src/engine/tensor.rs:59-63, :132-140).  Memory is NOT
+ * zero-filled (the reference zero-fills; call hs_memset where it matters). */
+HS_API hs_status hs_alloc(hs_ctx* ctx, size_t bytes, void** out);
+HS_API hs_status hs_free(hs_ctx* ctx, void* ptr);
+HS_API hs_status hs_memset(hs_ctx* ctx, void* dst, int value, size_t bytes);
+/* Replaces tensor_from_f32 upload (tensor.rs:66-89) and download (tensor.rs:163-198). */
+HS_API hs_status hs_memcpy_h2d(hs_ctx* ctx, void* dst_device, const void* src_host, size_t bytes);
+HS_API hs_status hs_memcpy_d2h(hs_ctx* ctx, void* dst_host, const void* src_device, size_t bytes);
+/* Replaces GpuContext::flush + sync (src/engine/mod.rs:261-284): waits for
+ * the stream and returns HS_ERR_TIMEOUT if a kernel's bounded wait fired. */
+HS_API hs_status hs_sync(hs_ctx* ctx);
+
+/* -------------------------------------------------------------- ops ---- */
+
+/* Replaces GpuContext::attention (src/engine/ops.rs:228-253).
+ * q, k, v, out: (S, H, T, D) of `dtype`; D must be 64; S*H <= 65535.
+ * scale <= 0 selects 1/sqrt(D) as the reference does (ops.rs:244).
+ * f16/bf16 inputs compute on tcgen05 in that type with f32 softmax;
+ * f32 inputs are rounded to bf16 for the tensor core, out stays f32. */
+HS_API hs_status hs_attention(hs_ctx* ctx, const void* q, const void* k, const void* v, void* out, uint32_t S, uint32_t H,
+                       uint32_t T, uint32_t D, hs_dtype dtype, float scale);
+
+/* The attention section of Block::forward (src/model/block.rs:136-148) as
+ * one op: QK-norm (LayerNorm over D with f32 weight/bias, eps) on q and k,
+ * then 2D RoPE (rotate-half, src/engine/rope.rs:48-55) on q and k, then
+ * attention.  The Q side runs inside the attention kernel's load prologue;
+ * K is normalised/rotated once into context scratch.
+ *   q_norm_w == NULL: no QK-norm (k_norm_w must then be NULL too).
+ *   rope_sin == NULL: no RoPE.  Otherwise the table row of token t is
+ *   (t mod tokens_per_frame) - prefix and tokens with (t mod tokens_per_frame)
+ *   < prefix pass through; tokens_per_frame == 0 means T (the reference's
+ *   rope_apply, ops.rs:202-223).  rope_rows >= tokens_per_frame - prefix. */
+HS_API hs_status hs_attention_fused(hs_ctx* ctx, const void* q, const void* k, const void* v, void* out, uint32_t S,
+                             uint32_t H, uint32_t T, uint32_t D, hs_dtype dtype, float scale, const float* q_norm_w,
+                             const float* q_norm_b, const float* k_norm_w, const float* k_norm_b, float eps,
+                             const float* rope_sin, const float* rope_cos, uint32_t rope_rows, uint32_t prefix,
+                             uint32_t tokens_per_frame);
+
+/* Replaces GpuContext::layernorm (src/engine/ops.rs:130-153), with eps an
+ * argument (the reference fixes 1e-5, ops.rs:139).  w, b: (dim) f32. */
+HS_API hs_status hs_layernorm(hs_ctx* ctx, const void* x, const float* w, const float* b, void* out, uint64_t rows,
+                       uint32_t dim, float eps, hs_dtype dtype);
+
+/* Replaces GpuContext::rope_apply (src/engine/ops.rs:202-223): in place on
+ * (S, H, T, D); tables (rope_rows, D) f32 with rope_rows == T - prefix. */
+HS_API hs_status hs_rope_apply(hs_ctx* ctx, void* x, const float* rope_sin, const float* rope_cos, uint32_t rope_rows,
+                        uint32_t S, uint32_t H, uint32_t T, uint32_t D, uint32_t prefix, hs_dtype dtype);
+
+/* Replaces GpuContext::split_heads (src/engine/ops.rs:185-200): (S*T, H*D) -> (S, H, T, D). */
+HS_API hs_status hs_split_heads(hs_ctx* ctx, const void* x, void* out, uint32_t S, uint32_t T, uint32_t H, uint32_t D,
+                         hs_dtype dtype);
+
+/* Replaces GpuContext::attn_merge (src/engine/ops.rs:255-267): (S, H, T, D) -> (S*T, H*D). */
+HS_API hs_status hs_attn_merge(hs_ctx* ctx, const void* x, void* out, uint32_t S, uint32_t H, uint32_t T, uint32_t D,
+                        hs_dtype dtype);
+
+/* ------------------------------------------------------ host helpers --- */
+
+/* Replaces rope::periods (src/engine/rope.rs:8-10): 100^(2i/32), i < 16. */
+HS_API hs_status hs_rope_periods(float* out16);
+
+/* Replaces rope::tables (src/engine/rope.rs:15-44): host (P, 64) sin/cos,
+ * P = h_p*w_p; periods == NULL uses hs_rope_periods. */
+HS_API hs_status hs_rope_tables(const float* periods, uint32_t h_p, uint32_t w_p, float* sin_out, float* cos_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HEADSHOT_CUDA_H */

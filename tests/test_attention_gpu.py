@@ -1,0 +1,178 @@
+"""Parity of the tcgen05 attention path against the CPU oracle (a
+restatement of shaders/attention.wesl, layernorm.wesl, rope_apply.wesl).
+
+Method: seeded f32 inputs are rounded to the storage dtype first, so the
+oracle and the GPU see identical values; the oracle computes in f32, the GPU
+on tensor cores in that dtype with f32 softmax statistics.  Gate (the
+north-star tolerance for bf16/fp16 compute): cosine >= 0.9999 and
+max |diff| <= 1e-2, NaN-proof (src/parity.rs:85-103).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from headshot_b200.engine import GpuContext, QkNorm, Rope
+
+pytestmark = pytest.mark.gpu
+
+TORCH = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}
+COS_MIN, ABS_MAX = 0.9999, 1e-2
+
+
+def dev(x: np.ndarray, dtype: str) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(x, np.float32)).cuda().to(TORCH[dtype])
+
+
+def host(t: torch.Tensor) -> np.ndarray:
+    return t.float().cpu().numpy()
+
+
+def rounded(x: np.ndarray, dtype: str) -> np.ndarray:
+    return x if dtype == "f32" else oracle.round_to(dtype, x)
+
+
+def gate(ours, ref, cos_min=COS_MIN, abs_max=ABS_MAX):
+    m = oracle.compare(ours, ref)
+    oracle.gate(m, cos_min, abs_max)
+    return m
+
+
+# ---- the reference's own known-answer cases (tests/kernels.rs:184-239) ----
+
+@pytest.mark.parametrize("t", [17, 64, 150])
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+def test_attention_kernels_rs_cases(gpu_ctx: GpuContext, t, dtype):
+    # S=2, H=3, D=64; SplitMix64 seed 5+T, q, k, v drawn in that order from one stream.
+    s, h, d = 2, 3, 64
+    vals = oracle.rng_uniform(5 + t, 3 * s * h * t * d)
+    q, k, v = (rounded(vals[i * s * h * t * d:(i + 1) * s * h * t * d].reshape(s, h, t, d), dtype) for i in range(3))
+    ref = oracle.attention(q, k, v)
+    out = gpu_ctx.attention(dev(q, dtype), dev(k, dtype), dev(v, dtype))
+    gpu_ctx.sync()
+    gate(host(out), ref)
+
+
+@pytest.mark.parametrize("t", [1, 2, 100, 127, 128, 129, 255, 256, 257, 383, 1374])
+def test_attention_tails_bf16(gpu_ctx, t):
+    s, h, d = 1, 2, 64
+    rng = np.random.default_rng(100 + t)
+    q, k, v = (rounded(rng.standard_normal((s, h, t, d), np.float32), "bf16") for _ in range(3))
+    ref = oracle.attention(q, k, v)
+    out = gpu_ctx.attention(dev(q, "bf16"), dev(k, "bf16"), dev(v, "bf16"))
+    gpu_ctx.sync()
+    gate(host(out), ref)
+
+
+def test_attention_f32_storage(gpu_ctx):
+    # f32 callers: tensor cores see bf16-rounded q, k, v; out stays f32.
+    s, h, t, d = 2, 2, 300, 64
+    rng = np.random.default_rng(7)
+    q, k, v = (rng.standard_normal((s, h, t, d), np.float32) for _ in range(3))
+    ref = oracle.attention(q, k, v)
+    out = gpu_ctx.attention(dev(q, "f32"), dev(k, "f32"), dev(v, "f32"))
+    gpu_ctx.sync()
+    assert out.dtype == torch.float32
+    gate(host(out), ref)
+
+
+# ---- fused QK-norm + RoPE (block.rs:136-148) --------------------------------
+
+def _fused_case(gpu_ctx, s, h, t, dtype, prefix, tpf, grid, seed, ln_random=True, rope=True):
+    d = 64
+    rng = np.random.default_rng(seed)
+    q, k, v = (rounded(rng.standard_normal((s, h, t, d), np.float32), dtype) for _ in range(3))
+    if ln_random:
+        qw, qb, kw, kb = (rng.uniform(0.5, 1.5, d).astype(np.float32), rng.uniform(-0.2, 0.2, d).astype(np.float32),
+                          rng.uniform(0.5, 1.5, d).astype(np.float32), rng.uniform(-0.2, 0.2, d).astype(np.float32))
+    else:
+        qw = kw = np.ones(d, np.float32)
+        qb = kb = np.zeros(d, np.float32)
+    eps = 1e-6
+    sin = cos = None
+    if rope:
+        sin, cos = oracle.rope_tables(*grid)
+    qn = oracle.qk_prep(q, qw, qb, eps, sin, cos, prefix, tpf)
+    kn = oracle.qk_prep(k, kw, kb, eps, sin, cos, prefix, tpf)
+    ref = oracle.attention(qn, kn, v)
+    c = lambda a: torch.from_numpy(a).cuda()  # noqa: E731
+    out = gpu_ctx.attention_fused(
+        dev(q, dtype), dev(k, dtype), dev(v, dtype), qk_norm=QkNorm(c(qw), c(qb), c(kw), c(kb), eps),
+        rope=Rope(c(sin), c(cos), prefix, tpf) if rope else None)
+    gpu_ctx.sync()
+    return host(out), ref
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+def test_fused_frame_reference_shape(gpu_ctx, dtype):
+    # Reference trunk frame block: prefix 17, P = 4x4 patches -> T = 33.
+    ours, ref = _fused_case(gpu_ctx, 3, 4, 33, dtype, prefix=17, tpf=33, grid=(4, 4), seed=11)
+    gate(ours, ref)
+
+
+def test_fused_frame_baseline_shape(gpu_ctx):
+    # BASELINE frame attention: 37x37 grid + 5 special tokens, T = 1374, fp16.
+    ours, ref = _fused_case(gpu_ctx, 2, 16, 1374, "f16", prefix=5, tpf=1374, grid=(37, 37), seed=2)
+    gate(ours, ref)
+
+
+def test_fused_global_multi_frame(gpu_ctx):
+    # Global attention over 3 frames of 1374 tokens with per-frame RoPE positions.
+    ours, ref = _fused_case(gpu_ctx, 1, 2, 3 * 1374, "bf16", prefix=5, tpf=1374, grid=(37, 37), seed=3,
+                            ln_random=False)
+    gate(ours, ref)
+
+
+def test_fused_no_rope(gpu_ctx):
+    ours, ref = _fused_case(gpu_ctx, 1, 3, 500, "bf16", prefix=0, tpf=500, grid=(1, 1), seed=4, rope=False)
+    gate(ours, ref)
+
+
+def test_fused_f32_storage(gpu_ctx):
+    ours, ref = _fused_case(gpu_ctx, 2, 2, 199, "f32", prefix=17, tpf=199, grid=(13, 14), seed=5)
+    gate(ours, ref)
+
+
+# ---- companion ops -----------------------------------------------------------
+
+@pytest.mark.parametrize("dtype", ["f32", "f16", "bf16"])
+def test_layernorm(gpu_ctx, dtype):
+    # kernels.rs:100-126 shape (19 x 300, dim > 256) plus the QK-norm shape.
+    for rows, dim, seed in ((19, 300, 3), (1000, 64, 4)):
+        x = rounded(oracle.rng_uniform(seed, rows * dim).reshape(rows, dim), dtype)
+        w = oracle.rng_uniform(seed + 100, dim)
+        b = oracle.rng_uniform(seed + 200, dim)
+        ref = oracle.layernorm(x, w, b, 1e-5)
+        out = gpu_ctx.layernorm(dev(x, dtype), torch.from_numpy(w).cuda(), torch.from_numpy(b).cuda())
+        gpu_ctx.sync()
+        tol = 1e-4 if dtype == "f32" else 2e-2 * max(1.0, float(np.abs(ref).max()))
+        assert np.abs(host(out) - ref).max() <= tol
+
+
+@pytest.mark.parametrize("dtype", ["f32", "f16", "bf16"])
+def test_rope_apply(gpu_ctx, dtype):
+    # kernels.rs:149-182: prefix 5 on a 2x3 grid, s=2, h=3, t=11.
+    s, h, t, d, prefix = 2, 3, 11, 64, 5
+    sin, cos = oracle.rope_tables(2, 3)
+    x = rounded(oracle.rng_uniform(4, s * h * t * d).reshape(s, h, t, d), dtype)
+    ref = oracle.rope_apply(x, sin, cos, prefix)
+    g = dev(x, dtype)
+    gpu_ctx.rope_apply(g, torch.from_numpy(sin).cuda(), torch.from_numpy(cos).cuda(), prefix)
+    gpu_ctx.sync()
+    tol = 1e-5 if dtype == "f32" else 2e-2
+    assert np.abs(host(g) - ref).max() <= tol * max(1.0, float(np.abs(ref).max()))
+
+
+@pytest.mark.parametrize("dtype", ["f32", "f16", "bf16"])
+def test_split_merge_roundtrip(gpu_ctx, dtype):
+    # kernels.rs:241-274, exact.
+    for s, t, h, d in ((2, 5, 4, 8), (3, 17, 16, 64)):
+        x = rounded(oracle.rng_uniform(6, s * t * h * d).reshape(s * t, h * d), dtype)
+        heads = gpu_ctx.split_heads(dev(x, dtype), s, t, h, d)
+        gpu_ctx.sync()
+        np.testing.assert_array_equal(host(heads), oracle.split_heads(x, s, t, h, d))
+        merged = gpu_ctx.attn_merge(heads)
+        gpu_ctx.sync()
+        np.testing.assert_array_equal(host(merged), x)
