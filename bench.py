@@ -1,0 +1,451 @@
+#!/usr/bin/env python
+"""bench.py — aggregator attention on B200 through libheadshot_cuda.so.
+
+Default workload (the metric's "global attention at 200
+frames"): one non-causal sequence of 200 x 1374 = 274,800 tokens, 16 heads
+x 64, bf16 q/k/v ~ N(0,1) (seed 3), fused QK-LayerNorm (w=1, b=0, eps 1e-6)
+and per-frame 2D RoPE (37x37 grid, 5 special tokens unrotated).  A step is
+one hs_attention_fused call over the whole sequence; at N GPUs it is the
+ring-parallel session call over N sequence shards (strong scaling).
+
+`--workload frame` runs config 3 (200 frames of 1374 tokens, fp16, frames
+sharded across ranks) and `--workload global43k` config 2.
+
+Prints ONE JSON line on rank 0.  `--impl reference` times the CPU
+restatement of the reference's f32 attention (oracle/, a port: the Rust/WGSL
+reference cannot run here) on the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "global-attn TFLOP/s (% bf16 peak) at 200 frames, 1/2/4/8 GPU; aggregator frames/s"
+
+WORKLOADS = {
+    "global": dict(S=1, H=16, frames=200, T_f=1374, dtype="bf16", seed=3, prefix=5, grid=(37, 37), eps=1e-6,
+                   name="global attention, 200 frames x 1374 tokens = 274,800 tokens, 16 heads x 64, bf16, "
+                        "fused QK-LayerNorm + per-frame 2D RoPE (37x37, 5 special tokens), non-causal"),
+    "global43k": dict(S=1, H=16, frames=32, T_f=1374, dtype="bf16", seed=1, prefix=5, grid=(37, 37), eps=1e-6,
+                      name="global attention, 32 frames x 1374 = 43,968 tokens, 16 heads x 64, bf16, "
+                           "fused QK-LayerNorm + per-frame 2D RoPE, non-causal"),
+    "frame": dict(S=200, H=16, frames=1, T_f=1374, dtype="f16", seed=2, prefix=5, grid=(37, 37), eps=1e-6,
+                  name="batched frame attention, 200 frames x 1374 tokens, 16 heads x 64, fp16, "
+                       "fused QK-LayerNorm + 2D RoPE (37x37, 5 special tokens)"),
+}
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"bf16": float(d["bf16_tflops"]), "bf16_sustained": float(d["bf16_tflops_sustained"]),
+                "source": "measured"}
+    return {"bf16": 1590.0, "bf16_sustained": 1400.0, "source": "fallback"}
+
+
+# --------------------------------------------------------------- clocks ---
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.gpu_id = gpu_id
+        self.lines: list[str] = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", self.gpu_id], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._pump, daemon=True)
+        self.thread.start()
+
+    def _pump(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=5)
+        sm, mx, power, reasons = [], 0.0, [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+                power.append(float(f[3]))
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm),
+                "power_w_median": statistics.median(power) if power else None}
+
+
+# ---------------------------------------------------------- CPU oracle ---
+
+def cpu_attention_sample(q_h, k_h, v_h, T, seconds_target: float, threads: int, prep: dict):
+    """Time the oracle's per-query online softmax (attention.wesl restated in C) on
+    sampled query rows of head 0 against all T keys: returns (TFLOP/s, rows, seconds)."""
+    import numpy as np
+
+    import oracle
+
+    sin, cos = oracle.rope_tables(*prep["grid"])
+    w = np.ones(64, np.float32)
+    b = np.zeros(64, np.float32)
+    qn = oracle.qk_prep(q_h, w, b, prep["eps"], sin, cos, prep["prefix"], prep["T_f"])
+    kn = oracle.qk_prep(k_h, w, b, prep["eps"], sin, cos, prep["prefix"], prep["T_f"])
+    rng = np.random.default_rng(0)
+    probe = rng.integers(0, T, threads)
+    t0 = time.perf_counter()
+    oracle.attention_rows(qn, kn, v_h, probe, nthreads=threads)
+    per_round = max(time.perf_counter() - t0, 1e-3)
+    rounds = max(1, int(seconds_target / per_round))
+    rows = rng.integers(0, T, rounds * threads)
+    t0 = time.perf_counter()
+    oracle.attention_rows(qn, kn, v_h, rows, nthreads=threads)
+    dt = time.perf_counter() - t0
+    flops = 4.0 * rows.size * T * 64
+    return flops / dt / 1e12, int(rows.size), dt
+
+
+# -------------------------------------------------------------- helpers ---
+
+def dist_setup():
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def gpu_id_for_smi(local: int) -> str:
+    import torch
+
+    try:
+        u = str(torch.cuda.get_device_properties(local).uuid)
+        return u if u.startswith("GPU-") else "GPU-" + u
+    except Exception:
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        if vis:
+            return vis.split(",")[local]
+        return str(local)
+
+
+# ------------------------------------------------------------ our arm ----
+
+def run_ours(args, wl: dict, rank: int, world: int, local: int) -> dict | None:
+    import numpy as np
+    import torch
+
+    import headshot_b200.rope as rope_mod
+    from headshot_b200.engine import GpuContext, QkNorm, Rope
+    from headshot_b200.session import shard_bounds
+
+    tdt = {"bf16": torch.bfloat16, "f16": torch.float16}[wl["dtype"]]
+    S, H, T_f, frames = wl["S"], wl["H"], wl["T_f"], wl["frames"]
+    T = T_f * frames
+    ctx = GpuContext(local)
+    dev = torch.device("cuda", local)
+
+    sin, cos = rope_mod.tables(None, *wl["grid"])
+    sin_d, cos_d = torch.from_numpy(sin).to(dev), torch.from_numpy(cos).to(dev)
+    w = torch.ones(64, device=dev)
+    b = torch.zeros(64, device=dev)
+    norm = QkNorm(w, b, w, b, wl["eps"])
+
+    if S > 1:  # frame attention: frames sharded across ranks, no communication
+        s0, s1 = shard_bounds(S, world, rank)
+        shape = (s1 - s0, H, T, 64)
+        flops_rank = 4.0 * (s1 - s0) * H * T * T * 64
+        flops_total = 4.0 * S * H * T * T * 64
+        session = None
+    else:  # global attention: sequence sharded, ring over ranks
+        t0, t1 = shard_bounds(T, world, rank)
+        shape = (1, H, t1 - t0, 64)
+        flops_rank = 4.0 * H * (t1 - t0) * T * 64
+        flops_total = 4.0 * H * T * T * 64
+        session = None
+        if world > 1:
+            from headshot_b200.session import RingSession
+
+            session = RingSession(ctx, rank, world)
+
+    g = torch.Generator(device=dev).manual_seed(wl["seed"] * 1000 + rank)
+    q, k, v = (torch.randn(shape, device=dev, dtype=torch.float32, generator=g).to(tdt) for _ in range(3))
+    out = torch.empty_like(q)
+    rope = Rope(sin_d, cos_d, wl["prefix"], T_f)
+
+    if session is None:
+        def step():
+            ctx.attention_fused(q, k, v, qk_norm=norm, rope=rope, out=out)
+    else:
+        def step():
+            session.attention_fused(q, k, v, out, T_total=T, qk_norm=norm, rope=rope)
+
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        step()
+    ctx.sync()
+    torch.cuda.synchronize(dev)
+
+    # ---- device-resident timed region --------------------------------
+    sampler = ClockSampler(gpu_id_for_smi(local))
+    sampler.start()
+    time.sleep(0.3)
+    ctx.prof_reset()
+    ctx.prof_enable(True)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    ctx.prof_enable(False)
+    clocks = sampler.stop()
+    ctx.sync()
+    ms_local = e0.elapsed_time(e1)
+    attn_ms, attn_n = ctx.prof_read("attention")
+    all_ms, all_n = ctx.prof_read("*")
+    ms = max_over_ranks(ms_local, world)
+    ms_per_step = ms / args.steps
+    value = flops_total / (ms_per_step / 1e3) / 1e12
+
+    # ---- end to end through the C ABI: pinned host in, host out -------
+    qh, kh, vh = (x.cpu().pin_memory() for x in (q, k, v))
+    oh = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    e2e_steps = max(1, min(args.steps, 5))
+
+    def e2e_step():
+        ctx.upload(q, qh)
+        ctx.upload(k, kh)
+        ctx.upload(v, vh)
+        step()
+        ctx.download(oh, out)
+
+    e2e_step()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    f0 = torch.cuda.Event(enable_timing=True)
+    f1 = torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    f1.record(stream)
+    torch.cuda.synchronize(dev)
+    ctx.sync()
+    e2e_ms = max_over_ranks(f0.elapsed_time(f1) / e2e_steps, world)
+    e2e_value = flops_total / (e2e_ms / 1e3) / 1e12
+    h2d = 3 * q.numel() * q.element_size() * world
+    d2h = out.numel() * out.element_size() * world
+
+    # ---- roofline of the dominant kernel (attention), live events ----
+    peaks = measured_peaks()
+    attn_per_launch_ms = attn_ms / max(attn_n, 1)
+    flops_per_launch = flops_rank if session is None else flops_rank / world
+    achieved = flops_per_launch / (attn_per_launch_ms / 1e3) / 1e12
+    roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peaks["bf16"], "unit": "TFLOP/s",
+                "frac": round(achieved / peaks["bf16"], 4), "traffic": None,
+                "peak_source": f"{peaks['source']} bf16 burst (MEASURED_PEAKS.json)",
+                "kernel": "attn_fwd_sm100", "kernel_ms_per_launch": round(attn_per_launch_ms, 3),
+                "launches": attn_n, "kernel_share_of_step": round(attn_ms / max(all_ms, 1e-9), 4)}
+
+    result = None
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline and S == 1:
+            head = lambda x: x[0, 0].float().cpu().numpy()[None, None]  # noqa: E731
+            tf, rows, dt = cpu_attention_sample(head(q), head(k), head(v), T, args.cpu_seconds,
+                                                args.cpu_threads or _threads(), dict(wl, T_f=T_f))
+            cpu = {"value": round(tf, 6), "unit": "TFLOP/s", "cores": args.cpu_threads or _threads(), "kind": "port",
+                   "sample": f"{rows} query rows of head 0 x all {T} keys (rows are independent), "
+                             f"fused QK-LN + RoPE on the CPU, {dt:.1f} s"}
+        result = {
+            "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": wl["dtype"],
+            "data": f"synthetic N(0,1) q/k/v, seed {wl['seed']}",
+            "config": {"workload": wl["name"], "S": S, "H": H, "T": T, "D": 64,
+                       "tokens": S * T, "tokens_per_s": round(S * T / (ms_per_step / 1e3), 1),
+                       "flops_per_step": flops_total,
+                       "frac_of_measured_bf16_peak": round(value / peaks["bf16"], 4),
+                       "parallelism": ("ring sequence-parallel" if S == 1 else "frame-sharded") + f" x{world}",
+                       "l2": "inputs larger than L2 (each of q/k/v > 126 MB); no flush needed"},
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_value, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3), "steps": e2e_steps},
+            "gpu_launches": int(all_n) * world,
+            "clocks": clocks,
+        }
+    if session is not None:
+        session.close()
+    ctx.close()
+    return result
+
+
+def _threads() -> int:
+    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+
+
+# ------------------------------------------------------ reference arm ----
+
+def run_reference(args, wl: dict) -> dict:
+    """The reference path's CPU implementation (oracle port of attention.wesl +
+    layernorm.wesl + rope_apply.wesl) on all host cores, bounded samples."""
+    import numpy as np
+
+    import oracle
+
+    S, H, T_f, frames = wl["S"], wl["H"], wl["T_f"], wl["frames"]
+    T = T_f * frames
+    threads = args.cpu_threads or _threads()
+    rng = np.random.default_rng(wl["seed"])
+    q, k, v = (oracle.round_to(wl["dtype"], rng.standard_normal((1, 1, T, 64), np.float32)) for _ in range(3))
+    sin, cos = oracle.rope_tables(*wl["grid"])
+    w = np.ones(64, np.float32)
+    b = np.zeros(64, np.float32)
+    # probe to size a step at ~ args.ref_step_seconds of CPU time
+    qn = oracle.qk_prep(q, w, b, wl["eps"], sin, cos, wl["prefix"], T_f)
+    kn = oracle.qk_prep(k, w, b, wl["eps"], sin, cos, wl["prefix"], T_f)
+    t0 = time.perf_counter()
+    oracle.attention_rows(qn, kn, v, rng.integers(0, T, threads), nthreads=threads)
+    per = max(time.perf_counter() - t0, 1e-3)
+    rows_per_step = threads * max(1, int(args.ref_step_seconds / per))
+
+    def step():
+        rows = rng.integers(0, T, rows_per_step)
+        qs = oracle.qk_prep(q, w, b, wl["eps"], sin, cos, wl["prefix"], T_f)
+        ks = oracle.qk_prep(k, w, b, wl["eps"], sin, cos, wl["prefix"], T_f)
+        oracle.attention_rows(qs, ks, v, rows, nthreads=threads)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = time.perf_counter() - t0
+    flops = 4.0 * rows_per_step * T * 64 * args.steps
+    value = flops / dt / 1e12
+    sample = (f"{rows_per_step} query rows x all {T} keys per step of one head (rows are independent), "
+              f"QK-LN + RoPE of that head's q/k each step; f32 per-query online softmax")
+    return {"impl": "reference", "metric": METRIC, "value": round(value, 6), "unit": "TFLOP/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": f"synthetic N(0,1), seed {wl['seed']}, rounded to {wl['dtype']}",
+            "config": {"workload": wl["name"], "S": S, "H": H, "T": T, "D": 64},
+            "cpu_baseline": {"value": round(value, 6), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="global")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--cpu-threads", type=int, default=0)
+    ap.add_argument("--ref-step-seconds", type=float, default=4.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        log("warmup raised to 3 (timing rule)")
+        args.warmup = 3
+    wl = WORKLOADS[args.workload]
+
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        if rank != 0:
+            return 0
+        print(json.dumps(run_reference(args, wl)), flush=True)
+        return 0
+
+    rank, world, local = dist_setup()
+    if world != args.gpus:
+        log(f"note: --gpus {args.gpus} but WORLD_SIZE {world}; using {world}")
+    try:
+        res = run_ours(args, wl, rank, world, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+    if res is not None:
+        print(json.dumps(res), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -53,6 +53,9 @@ SIGNATURES = {
     "hs_ctx_set_wait_timeout_ms": (_i, [_vp, _u32]),
     "hs_ctx_request_cancel": (_i, [_vp]),
     "hs_ctx_clear_cancel": (_i, [_vp]),
+    "hs_prof_enable": (_i, [_vp, _i]),
+    "hs_prof_reset": (_i, [_vp]),
+    "hs_prof_read": (_i, [_vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_u64)]),
     "hs_alloc": (_i, [_vp, ctypes.c_size_t, ctypes.POINTER(_vp)]),
     "hs_free": (_i, [_vp, _vp]),
     "hs_memset": (_i, [_vp, _vp, _i, ctypes.c_size_t]),

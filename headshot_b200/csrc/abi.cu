@@ -75,6 +75,25 @@ hs_status ctx_scratch(hs_ctx* ctx, size_t bytes, void** out) {
 
 uint64_t ctx_timeout_ns(hs_ctx* ctx) { return static_cast<uint64_t>(ctx->wait_timeout_ms) * 1000000ull; }
 
+ProfScope::ProfScope(hs_ctx* c, cudaStream_t s, const char* n) : ctx(c), st(s), name(n) {
+  if (!ctx || !ctx->prof_on) return;
+  for (cudaEvent_t* e : {&e0, &e1}) {
+    if (!ctx->prof_free.empty()) {
+      *e = ctx->prof_free.back();
+      ctx->prof_free.pop_back();
+    } else if (cudaEventCreate(e) != cudaSuccess) {
+      *e = nullptr;
+    }
+  }
+  if (e0) cudaEventRecord(e0, st);
+}
+
+ProfScope::~ProfScope() {
+  if (!e0 || !e1) return;
+  cudaEventRecord(e1, st);
+  ctx->prof.push_back(hs_prof_rec{name, e0, e1});
+}
+
 // Shared validation + dispatch of the attention family.
 hs_status attention_impl(hs_ctx* ctx, const void* q, const void* k, const void* v, void* out, uint32_t S, uint32_t H,
                          uint32_t T, uint32_t D, hs_dtype dtype, float scale, const QkPrologue& qp,
@@ -113,21 +132,31 @@ hs_status attention_impl(hs_ctx* ctx, const void* q, const void* k, const void* 
   uint8_t* cursor = static_cast<uint8_t*>(scratch);
   cudaError_t e;
   if (!k_direct) {
-    e = launch_qk_prep(st, k, code, cursor, elem, rows, T, kp);
+    {
+      ProfScope prof(ctx, st, "qk_prep");
+      e = launch_qk_prep(st, k, code, cursor, elem, rows, T, kp);
+    }
     if (e != cudaSuccess) return cuda_fail(e, "qk_prep(k)");
     k_use = cursor;
     cursor += tile_bytes;
   }
   if (!v_direct) {
     QkPrologue none{};
-    e = launch_qk_prep(st, v, code, cursor, elem, rows, T, none);
+    {
+      ProfScope prof(ctx, st, "qk_prep");
+      e = launch_qk_prep(st, v, code, cursor, elem, rows, T, none);
+    }
     if (e != cudaSuccess) return cuda_fail(e, "cast(v)");
     v_use = cursor;
   }
   std::string err;
   AttnState state{};
-  e = launch_attention_sm100(st, elem, q, code == kF32 ? kF32 : elem, k_use, v_use, out, code == kF32 ? kF32 : elem,
-                             S * H, T, T, scale, qp, state, ctx->d_status, ctx_timeout_ns(ctx), &err);
+  {
+    ProfScope prof(ctx, st, "attention");
+    e = launch_attention_sm100(st, elem, q, code == kF32 ? kF32 : elem, k_use, v_use, out,
+                               code == kF32 ? kF32 : elem, S * H, T, T, scale, qp, state, ctx->d_status,
+                               ctx_timeout_ns(ctx), &err);
+  }
   if (e != cudaSuccess) return fail(HS_ERR_CUDA, std::string(name) + ": " + (err.empty() ? cudaGetErrorString(e) : err));
   return HS_OK;
 }
@@ -181,6 +210,11 @@ hs_status hs_ctx_destroy(hs_ctx* ctx) {
   cudaStream_t st = ctx_stream(ctx);
   if (ctx->scratch) cudaFreeAsync(ctx->scratch, st);
   cudaStreamSynchronize(st);
+  for (auto& r : ctx->prof) {
+    cudaEventDestroy(r.start);
+    cudaEventDestroy(r.stop);
+  }
+  for (cudaEvent_t e : ctx->prof_free) cudaEventDestroy(e);
   cudaFree(ctx->d_status);
   cudaStreamDestroy(ctx->stream);
   delete ctx;
@@ -219,6 +253,45 @@ hs_status hs_ctx_request_cancel(hs_ctx* ctx) {
 hs_status hs_ctx_clear_cancel(hs_ctx* ctx) {
   if (!ctx) return fail(HS_ERR_INVALID, "hs_ctx_clear_cancel: null context");
   ctx->cancel.store(0);
+  return HS_OK;
+}
+
+hs_status hs_prof_enable(hs_ctx* ctx, int on) {
+  if (!ctx) return fail(HS_ERR_INVALID, "hs_prof_enable: null context");
+  ctx->prof_on = on != 0;
+  return HS_OK;
+}
+
+hs_status hs_prof_reset(hs_ctx* ctx) {
+  if (!ctx) return fail(HS_ERR_INVALID, "hs_prof_reset: null context");
+  DeviceGuard guard(ctx->device);
+  cudaStreamSynchronize(ctx_stream(ctx));
+  for (auto& r : ctx->prof) {
+    ctx->prof_free.push_back(r.start);
+    ctx->prof_free.push_back(r.stop);
+  }
+  ctx->prof.clear();
+  return HS_OK;
+}
+
+hs_status hs_prof_read(hs_ctx* ctx, const char* kernel, double* total_ms, uint64_t* launches) {
+  if (!ctx || !kernel || !total_ms || !launches) return fail(HS_ERR_INVALID, "hs_prof_read: null argument");
+  DeviceGuard guard(ctx->device);
+  double ms = 0.0;
+  uint64_t n = 0;
+  const bool all = strcmp(kernel, "*") == 0;
+  for (auto& r : ctx->prof) {
+    if (!all && r.kernel != kernel) continue;
+    cudaError_t e = cudaEventSynchronize(r.stop);
+    if (e != cudaSuccess) return cuda_fail(e, "hs_prof_read");
+    float one = 0.f;
+    e = cudaEventElapsedTime(&one, r.start, r.stop);
+    if (e != cudaSuccess) return cuda_fail(e, "hs_prof_read");
+    ms += one;
+    ++n;
+  }
+  *total_ms = ms;
+  *launches = n;
   return HS_OK;
 }
 
@@ -332,6 +405,7 @@ hs_status hs_layernorm(hs_ctx* ctx, const void* x, const float* w, const float* 
   if (rows == 0 || dim == 0) return HS_OK;
   if (!x || !w || !b || !out) return fail(HS_ERR_INVALID, "hs_layernorm: null pointer");
   DeviceGuard guard(ctx->device);
+  ProfScope prof(ctx, ctx_stream(ctx), "layernorm");
   cudaError_t e = launch_layernorm(ctx_stream(ctx), x, out, static_cast<int>(dtype), w, b, rows, dim, eps);
   return e == cudaSuccess ? HS_OK : cuda_fail(e, "hs_layernorm");
 }
@@ -348,8 +422,8 @@ hs_status hs_rope_apply(hs_ctx* ctx, void* x, const float* rope_sin, const float
   if (static_cast<uint64_t>(S) * H * T == 0) return HS_OK;
   if (!x || !rope_sin || !rope_cos) return fail(HS_ERR_INVALID, "hs_rope_apply: null pointer");
   DeviceGuard guard(ctx->device);
-  cudaError_t e =
-      launch_rope_apply(ctx_stream(ctx), x, static_cast<int>(dtype), rope_sin, rope_cos, S, H, T, D, prefix, T);
+  ProfScope prof(ctx, ctx_stream(ctx), "rope_apply");
+  cudaError_t e = launch_rope_apply(ctx_stream(ctx), x, static_cast<int>(dtype), rope_sin, rope_cos, S, H, T, D, prefix, T);
   return e == cudaSuccess ? HS_OK : cuda_fail(e, "hs_rope_apply");
 }
 
@@ -360,6 +434,7 @@ hs_status hs_split_heads(hs_ctx* ctx, const void* x, void* out, uint32_t S, uint
   if (static_cast<uint64_t>(S) * H * T * D == 0) return HS_OK;
   if (!x || !out) return fail(HS_ERR_INVALID, "hs_split_heads: null pointer");
   DeviceGuard guard(ctx->device);
+  ProfScope prof(ctx, ctx_stream(ctx), "permute");
   cudaError_t e = launch_split_heads(ctx_stream(ctx), x, out, static_cast<int>(dtype), S, T, H, D);
   return e == cudaSuccess ? HS_OK : cuda_fail(e, "hs_split_heads");
 }
@@ -371,6 +446,7 @@ hs_status hs_attn_merge(hs_ctx* ctx, const void* x, void* out, uint32_t S, uint3
   if (static_cast<uint64_t>(S) * H * T * D == 0) return HS_OK;
   if (!x || !out) return fail(HS_ERR_INVALID, "hs_attn_merge: null pointer");
   DeviceGuard guard(ctx->device);
+  ProfScope prof(ctx, ctx_stream(ctx), "permute");
   cudaError_t e = launch_attn_merge(ctx_stream(ctx), x, out, static_cast<int>(dtype), S, H, T, D);
   return e == cudaSuccess ? HS_OK : cuda_fail(e, "hs_attn_merge");
 }

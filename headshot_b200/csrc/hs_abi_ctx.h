@@ -6,8 +6,16 @@
 
 #include <atomic>
 #include <string>
+#include <vector>
 
 #include "../../include/headshot_cuda.h"
+
+// One bracketed kernel launch recorded while profiling is on.
+struct hs_prof_rec {
+  std::string kernel;
+  cudaEvent_t start;
+  cudaEvent_t stop;
+};
 
 struct hs_ctx {
   int device = 0;
@@ -20,7 +28,22 @@ struct hs_ctx {
   size_t scratch_bytes = 0;
   uint32_t wait_timeout_ms = 2000;
   std::atomic<int> cancel{0};
+  bool prof_on = false;
+  std::vector<hs_prof_rec> prof;     // recorded launches, oldest first
+  std::vector<cudaEvent_t> prof_free;  // recycled events
 };
+
+namespace hs {
+// Brackets one kernel launch with events when profiling is on.
+struct ProfScope {
+  hs_ctx* ctx;
+  cudaStream_t st;
+  const char* name;
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  ProfScope(hs_ctx* c, cudaStream_t s, const char* n);
+  ~ProfScope();
+};
+}  // namespace hs
 
 namespace hs {
 hs_status abi_fail(hs_status s, const std::string& msg);

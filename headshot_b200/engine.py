@@ -202,3 +202,33 @@ class GpuContext:
 
     def set_wait_timeout_ms(self, ms: int) -> None:
         check(self._L.hs_ctx_set_wait_timeout_ms(self._h, int(ms)))
+
+    # ---------------------------------------------------- profiling ----
+
+    def prof_enable(self, on: bool = True) -> None:
+        """Bracket every launch with CUDA events on its stream."""
+        check(self._L.hs_prof_enable(self._h, 1 if on else 0))
+
+    def prof_reset(self) -> None:
+        check(self._L.hs_prof_reset(self._h))
+
+    def prof_read(self, kernel: str = "*") -> tuple[float, int]:
+        """(summed device ms, launches) of `kernel` since the last reset."""
+        ms = ctypes.c_double()
+        n = ctypes.c_uint64()
+        check(self._L.hs_prof_read(self._h, kernel.encode(), ctypes.byref(ms), ctypes.byref(n)))
+        return ms.value, n.value
+
+    # ------------------------------------------- host <-> device (C ABI) --
+
+    def upload(self, dst: torch.Tensor, src: torch.Tensor) -> None:
+        """hs_memcpy_h2d of a contiguous host tensor into a device tensor."""
+        assert src.numel() * src.element_size() == dst.numel() * dst.element_size()
+        self._bind_stream()
+        check(self._L.hs_memcpy_h2d(self._h, _ptr(dst), _ptr(src), dst.numel() * dst.element_size()))
+
+    def download(self, dst: torch.Tensor, src: torch.Tensor) -> None:
+        """hs_memcpy_d2h of a device tensor into a contiguous host tensor."""
+        assert src.numel() * src.element_size() == dst.numel() * dst.element_size()
+        self._bind_stream()
+        check(self._L.hs_memcpy_d2h(self._h, _ptr(dst), _ptr(src), dst.numel() * dst.element_size()))

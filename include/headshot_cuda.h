@@ -79,6 +79,15 @@ HS_API hs_status hs_ctx_set_wait_timeout_ms(hs_ctx* ctx, uint32_t ms);
 HS_API hs_status hs_ctx_request_cancel(hs_ctx* ctx);
 HS_API hs_status hs_ctx_clear_cancel(hs_ctx* ctx);
 
+/* Per-kernel timing (the reference's unused TIMESTAMP_QUERY, mod.rs:137):
+ * when enabled, every kernel launch is bracketed by CUDA events on its
+ * stream.  hs_prof_read synchronises and returns the summed device time and
+ * launch count of `kernel` ("attention", "qk_prep", "layernorm",
+ * "rope_apply", "permute", or "*" for all). */
+HS_API hs_status hs_prof_enable(hs_ctx* ctx, int on);
+HS_API hs_status hs_prof_reset(hs_ctx* ctx);
+HS_API hs_status hs_prof_read(hs_ctx* ctx, const char* kernel, double* total_ms, uint64_t* launches);
+
 /* ------------------------------------------------------------- memory --- */
 
 /* Stream-ordered device pool; replaces GpuContext::empty_typed /
