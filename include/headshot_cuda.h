@@ -129,6 +129,30 @@ HS_API hs_status hs_attention_fused(hs_ctx* ctx, const void* q, const void* k, c
                              const float* rope_sin, const float* rope_cos, uint32_t rope_rows, uint32_t prefix,
                              uint32_t tokens_per_frame);
 
+/* No counterpart in the reference.  hs_attention_fused for callers that
+ * cannot let the library allocate device memory: hosts whose device memory
+ * belongs to their own allocator or a pool reserved up front, and session
+ * loops that must not stall or fail on an allocation once running.  Same
+ * arguments and results as hs_attention_fused (f16/bf16 storage only), but
+ * no hs_ctx: work goes on `stream` (a cudaStream_t, NULL = legacy default
+ * stream) of the current device, and the normalised K lives in a fixed
+ * array inside the library — HS_NOALLOC_MAX_ROWS rows of 128 bytes (32 MiB),
+ * held by every GPU that loads the library until the process exits.
+ * S*H*T above HS_NOALLOC_MAX_ROWS returns HS_ERR_INVALID.
+ * The first call on a device looks up that array's device address (no
+ * allocation by this library); make that first call before any stream
+ * capture.  All calls on a device share the array, so calls whose work
+ * overlaps on the GPU race; order them on one stream.  `status` (device
+ * int, may be NULL) is zeroed by each call and receives a nonzero site
+ * code if an in-kernel wait timed out. */
+#define HS_NOALLOC_MAX_ROWS 262144u
+HS_API hs_status hs_attention_fused_noalloc(void* stream, int* status, const void* q, const void* k, const void* v,
+                                            void* out, uint32_t S, uint32_t H, uint32_t T, uint32_t D,
+                                            hs_dtype dtype, float scale, const float* q_norm_w,
+                                            const float* q_norm_b, const float* k_norm_w, const float* k_norm_b,
+                                            float eps, const float* rope_sin, const float* rope_cos,
+                                            uint32_t rope_rows, uint32_t prefix, uint32_t tokens_per_frame);
+
 /* Replaces GpuContext::layernorm (src/engine/ops.rs:130-153), with eps an
  * argument (the reference fixes 1e-5, ops.rs:139).  w, b: (dim) f32. */
 HS_API hs_status hs_layernorm(hs_ctx* ctx, const void* x, const float* w, const float* b, void* out, uint64_t rows,
