@@ -95,7 +95,7 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
 }
 
 // 3-D tiled load into this CTA's shared memory; completion is signalled as
-// transaction bytes on `bar`.  No multicast.
+// transaction bytes on `bar`.  Single-CTA destination only.
 __device__ __forceinline__ void tma_load_3d(const CUtensorMap* map, uint64_t* bar, void* dst, int c0, int c1,
                                             int c2) {
   asm volatile(

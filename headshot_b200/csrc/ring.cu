@@ -1,0 +1,370 @@
+// ring.cu — sequence-parallel (ring) global attention across GPUs.
+//
+// The reference runs global attention as one streaming kernel over N·T
+// tokens on one device (src/model/trunk.rs:124-125); this is the new
+// multi-GPU session layer.  Each rank owns a contiguous shard of the
+// sequence (all heads): q, k, v, out are (H, T_r, 64) with T_r from
+// hs_ring_shard.  K' = RoPE(LN(K)) is computed once per shard by its owner,
+// then [K' | V] blocks travel around the ring with NCCL send/recv on a
+// communication stream while the tcgen05 kernel processes the block that
+// arrived in the previous step.  The running softmax state (unnormalised O,
+// max m, sum l — f32) stays on the rank and is carried from step to step by
+// the kernel itself; the last step writes the normalised output.
+//
+// NCCL is resolved at run time (dlopen "libnccl.so.2"), so the library loads
+// and the single-GPU ops work without it.
+#include <dlfcn.h>
+#include <math.h>
+#include <nccl.h>
+#include <string.h>
+
+#include <chrono>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <type_traits>
+
+#include "../../include/headshot_cuda.h"
+#include "hs_abi_ctx.h"
+#include "hs_internal.h"
+
+namespace {
+
+struct NcclApi {
+  bool loaded = false;
+  std::string error;
+  ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+  ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
+  ncclResult_t (*Send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*Recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*GroupStart)() = nullptr;
+  ncclResult_t (*GroupEnd)() = nullptr;
+  const char* (*GetErrorString)(ncclResult_t) = nullptr;
+};
+
+NcclApi& nccl() {
+  static NcclApi api;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) {
+      api.error = std::string("cannot load libnccl.so.2: ") + dlerror();
+      return;
+    }
+    bool ok = true;
+    auto sym = [&](auto& fn, const char* name) {
+      fn = reinterpret_cast<std::remove_reference_t<decltype(fn)>>(dlsym(h, name));
+      if (!fn) ok = false;
+    };
+    sym(api.GetUniqueId, "ncclGetUniqueId");
+    sym(api.CommInitRank, "ncclCommInitRank");
+    sym(api.CommDestroy, "ncclCommDestroy");
+    sym(api.CommAbort, "ncclCommAbort");
+    sym(api.CommGetAsyncError, "ncclCommGetAsyncError");
+    sym(api.Send, "ncclSend");
+    sym(api.Recv, "ncclRecv");
+    sym(api.GroupStart, "ncclGroupStart");
+    sym(api.GroupEnd, "ncclGroupEnd");
+    sym(api.GetErrorString, "ncclGetErrorString");
+    if (!ok) {
+      api.error = "libnccl.so.2 lacks a required symbol";
+      return;
+    }
+    api.loaded = true;
+  });
+  return api;
+}
+
+hs_status nccl_fail(ncclResult_t r, const char* what) {
+  NcclApi& n = nccl();
+  return hs::abi_fail(HS_ERR_NCCL, std::string(what) + ": " + (n.GetErrorString ? n.GetErrorString(r) : "nccl error"));
+}
+
+void shard(uint32_t n, int world, int rank, uint32_t* start, uint32_t* len) {
+  const uint32_t base = n / static_cast<uint32_t>(world);
+  const uint32_t rem = n % static_cast<uint32_t>(world);
+  const uint32_t r = static_cast<uint32_t>(rank);
+  *start = r * base + (r < rem ? r : rem);
+  *len = base + (r < rem ? 1u : 0u);
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+struct hs_ring {
+  hs_ctx* ctx = nullptr;
+  int rank = 0;
+  int world = 1;
+  ncclComm_t comm = nullptr;
+  cudaStream_t comm_stream = nullptr;
+  cudaEvent_t ev_block0 = nullptr;
+  cudaEvent_t ev_recv[2] = {nullptr, nullptr};
+  cudaEvent_t ev_compute[2] = {nullptr, nullptr};
+  cudaEvent_t ev_done = nullptr;
+  void* buf[2] = {nullptr, nullptr};
+  size_t buf_bytes = 0;
+  float* state = nullptr;  // o (rows x 64) | m (rows) | l (rows)
+  size_t state_rows = 0;
+  bool aborted = false;
+};
+
+extern "C" {
+
+hs_status hs_ring_shard(uint32_t n, int world, int rank, uint32_t* start, uint32_t* len) {
+  if (world < 1 || rank < 0 || rank >= world || !start || !len)
+    return hs::abi_fail(HS_ERR_INVALID, "hs_ring_shard: bad arguments");
+  shard(n, world, rank, start, len);
+  return HS_OK;
+}
+
+hs_status hs_ring_plan(int rank, int world, int step, int* src_block, int* send_to, int* recv_from,
+                       int* load_state, int* store_state) {
+  if (world < 1 || rank < 0 || rank >= world || step < 0 || step >= world)
+    return hs::abi_fail(HS_ERR_INVALID, "hs_ring_plan: bad arguments");
+  if (src_block) *src_block = (rank - step + world) % world;
+  const bool last = step == world - 1;
+  if (send_to) *send_to = last ? -1 : (rank + 1) % world;
+  if (recv_from) *recv_from = last ? -1 : (rank - 1 + world) % world;
+  if (load_state) *load_state = step > 0 ? 1 : 0;
+  if (store_state) *store_state = last ? 0 : 1;
+  return HS_OK;
+}
+
+size_t hs_ring_id_bytes(void) { return NCCL_UNIQUE_ID_BYTES; }
+
+hs_status hs_ring_unique_id(void* id_out) {
+  if (!id_out) return hs::abi_fail(HS_ERR_INVALID, "hs_ring_unique_id: null out");
+  NcclApi& n = nccl();
+  if (!n.loaded) return hs::abi_fail(HS_ERR_NCCL, n.error);
+  ncclUniqueId id;
+  ncclResult_t r = n.GetUniqueId(&id);
+  if (r != ncclSuccess) return nccl_fail(r, "ncclGetUniqueId");
+  memcpy(id_out, &id, sizeof id);
+  return HS_OK;
+}
+
+hs_status hs_ring_create(hs_ctx* ctx, int rank, int world, const void* id, hs_ring** out) {
+  if (!ctx || !id || !out || world < 1 || rank < 0 || rank >= world)
+    return hs::abi_fail(HS_ERR_INVALID, "hs_ring_create: bad arguments");
+  *out = nullptr;
+  NcclApi& n = nccl();
+  if (!n.loaded) return hs::abi_fail(HS_ERR_NCCL, n.error);
+  cudaSetDevice(ctx->device);
+  hs_ring* ring = new hs_ring();
+  ring->ctx = ctx;
+  ring->rank = rank;
+  ring->world = world;
+  ncclUniqueId uid;
+  memcpy(&uid, id, sizeof uid);
+  ncclResult_t r = n.CommInitRank(&ring->comm, world, uid, rank);
+  if (r != ncclSuccess) {
+    delete ring;
+    return nccl_fail(r, "ncclCommInitRank");
+  }
+  cudaError_t e = cudaStreamCreateWithFlags(&ring->comm_stream, cudaStreamNonBlocking);
+  for (cudaEvent_t* ev : {&ring->ev_block0, &ring->ev_recv[0], &ring->ev_recv[1], &ring->ev_compute[0],
+                          &ring->ev_compute[1], &ring->ev_done})
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(ev, cudaEventDisableTiming);
+  if (e != cudaSuccess) {
+    n.CommDestroy(ring->comm);
+    delete ring;
+    return hs::abi_cuda_fail(e, "hs_ring_create");
+  }
+  *out = ring;
+  return HS_OK;
+}
+
+hs_status hs_ring_destroy(hs_ring* ring) {
+  if (!ring) return HS_OK;
+  NcclApi& n = nccl();
+  cudaSetDevice(ring->ctx->device);
+  if (!ring->aborted) {
+    cudaStreamSynchronize(ring->comm_stream);
+    cudaStreamSynchronize(hs::ctx_stream(ring->ctx));
+  }
+  if (ring->comm) {
+    if (ring->aborted)
+      n.CommAbort(ring->comm);
+    else
+      n.CommDestroy(ring->comm);
+  }
+  for (void* b : ring->buf)
+    if (b) cudaFree(b);
+  if (ring->state) cudaFree(ring->state);
+  for (cudaEvent_t ev : {ring->ev_block0, ring->ev_recv[0], ring->ev_recv[1], ring->ev_compute[0],
+                         ring->ev_compute[1], ring->ev_done})
+    if (ev) cudaEventDestroy(ev);
+  if (ring->comm_stream) cudaStreamDestroy(ring->comm_stream);
+  delete ring;
+  return HS_OK;
+}
+
+hs_status hs_ring_attention_fused(hs_ring* ring, const void* q, const void* k, const void* v, void* out, uint32_t H,
+                                  uint32_t T_total, uint32_t D, hs_dtype dtype, float scale, const float* q_norm_w,
+                                  const float* q_norm_b, const float* k_norm_w, const float* k_norm_b, float eps,
+                                  const float* rope_sin, const float* rope_cos, uint32_t rope_rows, uint32_t prefix,
+                                  uint32_t tokens_per_frame) {
+  const char* name = "hs_ring_attention_fused";
+  if (!ring) return hs::abi_fail(HS_ERR_INVALID, std::string(name) + ": null ring");
+  if (ring->aborted) return hs::abi_fail(HS_ERR_NCCL, std::string(name) + ": ring was aborted");
+  hs_ctx* ctx = ring->ctx;
+  const int R = ring->world, r = ring->rank;
+  if (ctx->cancel.load()) return hs::abi_fail(HS_ERR_CANCELLED, std::string(name) + ": cancelled");
+  if (dtype != HS_F16 && dtype != HS_BF16)
+    return hs::abi_fail(HS_ERR_UNSUPPORTED, std::string(name) + ": ring path takes f16/bf16 storage");
+  if (D != 64) return hs::abi_fail(HS_ERR_UNSUPPORTED, std::string(name) + ": head_dim must be 64");
+  if (H == 0 || H > 65535 || T_total < static_cast<uint32_t>(R))
+    return hs::abi_fail(HS_ERR_INVALID, std::string(name) + ": need 1 <= H <= 65535 and T_total >= world");
+  uint32_t t0, tr;
+  shard(T_total, R, r, &t0, &tr);
+  if (!q || !k || !v || !out) return hs::abi_fail(HS_ERR_INVALID, std::string(name) + ": null tensor pointer");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
+    return hs::abi_fail(HS_ERR_INVALID, std::string(name) + ": tensor pointers must be 16-byte aligned");
+  const bool ln = q_norm_w != nullptr;
+  if (ln != (k_norm_w != nullptr) || (ln && (!q_norm_b || !k_norm_b)))
+    return hs::abi_fail(HS_ERR_INVALID, std::string(name) + ": QK-norm needs all of q/k weight and bias, or none");
+  const bool rope = rope_sin != nullptr;
+  const uint32_t tpf = tokens_per_frame ? tokens_per_frame : T_total;
+  if (rope && (!rope_cos || prefix > tpf || rope_rows < tpf - prefix || !aligned16(rope_sin) || !aligned16(rope_cos)))
+    return hs::abi_fail(HS_ERR_INVALID, std::string(name) + ": bad RoPE tables / prefix");
+  if (!(scale > 0.f) || !isfinite(scale)) scale = 1.0f / sqrtf(static_cast<float>(D));
+
+  cudaSetDevice(ctx->device);
+  NcclApi& n = nccl();
+  cudaStream_t st = hs::ctx_stream(ctx);
+  cudaStream_t cs = ring->comm_stream;
+  const int code = static_cast<int>(dtype);
+  const size_t row_bytes = 64 * 2;
+  const uint32_t tmax = (T_total + R - 1) / R;
+  const size_t need_buf = 2ull * H * tmax * row_bytes;
+  cudaError_t e;
+  if (ring->buf_bytes < need_buf && R > 1) {
+    cudaStreamSynchronize(st);
+    cudaStreamSynchronize(cs);
+    for (void*& b : ring->buf) {
+      if (b) cudaFree(b);
+      b = nullptr;
+      e = cudaMalloc(&b, need_buf);
+      if (e != cudaSuccess) return hs::abi_cuda_fail(e, "ring buffers");
+    }
+    ring->buf_bytes = need_buf;
+  }
+  const size_t rows = static_cast<size_t>(H) * tr;
+  if (ring->state_rows < rows && R > 1) {
+    cudaStreamSynchronize(st);
+    if (ring->state) cudaFree(ring->state);
+    ring->state = nullptr;
+    e = cudaMalloc(&ring->state, rows * 66 * sizeof(float));
+    if (e != cudaSuccess) return hs::abi_cuda_fail(e, "ring state");
+    ring->state_rows = rows;
+  }
+
+  hs::QkPrologue qp{};
+  qp.ln = ln;
+  qp.ln_w = q_norm_w;
+  qp.ln_b = q_norm_b;
+  qp.eps = eps;
+  qp.rope = rope;
+  qp.sin_t = rope_sin;
+  qp.cos_t = rope_cos;
+  qp.prefix = prefix;
+  qp.tokens_per_frame = tpf;
+  qp.pos_offset = t0;
+  hs::QkPrologue kp = qp;
+  kp.ln_w = k_norm_w;
+  kp.ln_b = k_norm_b;
+
+  if (R == 1) {  // nothing to exchange: the single-device fused op
+    return hs_attention_fused(ctx, q, k, v, out, 1, H, T_total, D, dtype, scale, q_norm_w, q_norm_b, k_norm_w,
+                              k_norm_b, eps, rope_sin, rope_cos, rope_rows, prefix, tokens_per_frame);
+  }
+
+  // Block 0 = this rank's [K' | V] in buf[0].
+  uint8_t* b0 = static_cast<uint8_t*>(ring->buf[0]);
+  {
+    hs::ProfScope prof(ctx, st, "qk_prep");
+    e = (ln || rope) ? hs::launch_qk_prep(st, k, code, b0, code, rows, tr, kp)
+                     : cudaMemcpyAsync(b0, k, rows * row_bytes, cudaMemcpyDeviceToDevice, st);
+  }
+  if (e != cudaSuccess) return hs::abi_cuda_fail(e, "ring K' prep");
+  e = cudaMemcpyAsync(b0 + rows * row_bytes, v, rows * row_bytes, cudaMemcpyDeviceToDevice, st);
+  if (e != cudaSuccess) return hs::abi_cuda_fail(e, "ring V copy");
+  cudaEventRecord(ring->ev_block0, st);
+
+  hs::AttnState state{};
+  state.o = ring->state;
+  state.m = ring->state + rows * 64;
+  state.l = ring->state + rows * 65;
+  for (int s = 0; s < R; ++s) {
+    int src, send_to, recv_from, load, store;
+    hs_ring_plan(r, R, s, &src, &send_to, &recv_from, &load, &store);
+    uint32_t src_t0, src_len;
+    shard(T_total, R, src, &src_t0, &src_len);
+    uint8_t* cur = static_cast<uint8_t*>(ring->buf[s % 2]);
+    uint8_t* nxt = static_cast<uint8_t*>(ring->buf[(s + 1) % 2]);
+    if (send_to >= 0) {
+      const int nsrc = (src - 1 + R) % R;  // the block the previous rank holds now
+      uint32_t n_t0, n_len;
+      shard(T_total, R, nsrc, &n_t0, &n_len);
+      if (s == 0) cudaStreamWaitEvent(cs, ring->ev_block0, 0);
+      if (s >= 1) cudaStreamWaitEvent(cs, ring->ev_compute[(s - 1) % 2], 0);  // nxt was read by step s-1
+      ncclResult_t nr = n.GroupStart();
+      if (nr == ncclSuccess) nr = n.Send(cur, 2ull * H * src_len * row_bytes, ncclUint8, send_to, ring->comm, cs);
+      if (nr == ncclSuccess) nr = n.Recv(nxt, 2ull * H * n_len * row_bytes, ncclUint8, recv_from, ring->comm, cs);
+      ncclResult_t ge = n.GroupEnd();
+      if (nr != ncclSuccess) return nccl_fail(nr, "ring send/recv");
+      if (ge != ncclSuccess) return nccl_fail(ge, "ring group");
+      cudaEventRecord(ring->ev_recv[s % 2], cs);
+    }
+    if (s >= 1) cudaStreamWaitEvent(st, ring->ev_recv[(s - 1) % 2], 0);
+    state.load = load;
+    state.store = store;
+    std::string err;
+    {
+      hs::ProfScope prof(ctx, st, "attention");
+      e = hs::launch_attention_sm100(st, code, q, code, cur, cur + static_cast<size_t>(H) * src_len * row_bytes,
+                                     out, code, H, tr, src_len, scale, qp, state, ctx->d_status,
+                                     hs::ctx_timeout_ns(ctx), &err);
+    }
+    if (e != cudaSuccess)
+      return hs::abi_fail(HS_ERR_CUDA, std::string(name) + ": " + (err.empty() ? cudaGetErrorString(e) : err));
+    cudaEventRecord(ring->ev_compute[s % 2], st);
+  }
+  cudaEventRecord(ring->ev_done, st);
+  return HS_OK;
+}
+
+hs_status hs_ring_sync(hs_ring* ring, uint32_t timeout_ms) {
+  if (!ring) return hs::abi_fail(HS_ERR_INVALID, "hs_ring_sync: null ring");
+  if (ring->aborted) return hs::abi_fail(HS_ERR_NCCL, "hs_ring_sync: ring was aborted");
+  NcclApi& n = nccl();
+  cudaSetDevice(ring->ctx->device);
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    cudaError_t q1 = cudaStreamQuery(ring->comm_stream);
+    cudaError_t q2 = cudaStreamQuery(hs::ctx_stream(ring->ctx));
+    if (q1 == cudaSuccess && q2 == cudaSuccess) break;
+    if ((q1 != cudaSuccess && q1 != cudaErrorNotReady) || (q2 != cudaSuccess && q2 != cudaErrorNotReady))
+      return hs::abi_cuda_fail(q1 != cudaSuccess && q1 != cudaErrorNotReady ? q1 : q2, "hs_ring_sync");
+    ncclResult_t async_err = ncclSuccess;
+    n.CommGetAsyncError(ring->comm, &async_err);
+    const double waited =
+        std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    if ((async_err != ncclSuccess && async_err != ncclInProgress) || waited > timeout_ms) {
+      n.CommAbort(ring->comm);
+      ring->comm = nullptr;
+      ring->aborted = true;
+      if (async_err != ncclSuccess && async_err != ncclInProgress) return nccl_fail(async_err, "hs_ring_sync");
+      return hs::abi_fail(HS_ERR_TIMEOUT, "hs_ring_sync: ring did not finish in time; communicator aborted");
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(200));
+  }
+  return hs_sync(ring->ctx);
+}
+
+}  // extern "C"

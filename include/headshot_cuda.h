@@ -171,6 +171,42 @@ HS_API hs_status hs_split_heads(hs_ctx* ctx, const void* x, void* out, uint32_t 
 HS_API hs_status hs_attn_merge(hs_ctx* ctx, const void* x, void* out, uint32_t S, uint32_t H, uint32_t T, uint32_t D,
                         hs_dtype dtype);
 
+/* --------------------------------------- multi-GPU session (ring) ------ */
+
+/* The reference is single-device; this layer is new.  Global attention over
+ * one sequence of T_total tokens is split into `world` contiguous shards
+ * (hs_ring_shard); rank r owns q, k, v, out of shape (H, T_r, 64).  K is
+ * normalised/rotated once by its owner, then [K'|V] blocks rotate around the
+ * ring over NCCL send/recv, overlapped with the attention kernel; the
+ * running softmax state stays on each rank in f32. */
+typedef struct hs_ring hs_ring;
+
+/* [start, start+len) of rank's shard; the first n % world ranks get one extra token. */
+HS_API hs_status hs_ring_shard(uint32_t n, int world, int rank, uint32_t* start, uint32_t* len);
+/* Step `step` of the ring on `rank`: which block it attends to, its peers
+ * (-1 on the last step: nothing to send), and whether the kernel loads /
+ * stores the carried softmax state. */
+HS_API hs_status hs_ring_plan(int rank, int world, int step, int* src_block, int* send_to, int* recv_from,
+                              int* load_state, int* store_state);
+HS_API size_t hs_ring_id_bytes(void);
+/* Rank 0 creates the id and shares its bytes with the other ranks out of band. */
+HS_API hs_status hs_ring_unique_id(void* id_out);
+/* Collective over all ranks; one rank per GPU, ctx bound to that GPU. */
+HS_API hs_status hs_ring_create(hs_ctx* ctx, int rank, int world, const void* id, hs_ring** out);
+HS_API hs_status hs_ring_destroy(hs_ring* ring);
+/* Global attention over the ring, arguments as hs_attention_fused with
+ * S = 1; RoPE positions use each token's global index. f16/bf16 only. */
+HS_API hs_status hs_ring_attention_fused(hs_ring* ring, const void* q, const void* k, const void* v, void* out,
+                                         uint32_t H, uint32_t T_total, uint32_t D, hs_dtype dtype, float scale,
+                                         const float* q_norm_w, const float* q_norm_b, const float* k_norm_w,
+                                         const float* k_norm_b, float eps, const float* rope_sin,
+                                         const float* rope_cos, uint32_t rope_rows, uint32_t prefix,
+                                         uint32_t tokens_per_frame);
+/* Waits for the ring's work with a host-side watchdog: on an NCCL async
+ * error or after timeout_ms the communicator is aborted and the ring
+ * becomes unusable (HS_ERR_NCCL / HS_ERR_TIMEOUT). */
+HS_API hs_status hs_ring_sync(hs_ring* ring, uint32_t timeout_ms);
+
 /* ------------------------------------------------------ host helpers --- */
 
 /* Replaces rope::periods (src/engine/rope.rs:8-10): 100^(2i/32), i < 16. */
