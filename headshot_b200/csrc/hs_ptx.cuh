@@ -61,11 +61,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Bounded wait for the phase with parity `parity` to complete.
 // Returns false on timeout or when the CTA abort flag is up.  The first
-// kFastSpins polls touch nothing else: reading %globaltimer on the first
-// miss doubled the latency of an isolated mbarrier round trip (492 vs 228
-// cycles on B200), while long spins steal issue slots from warps that share
-// the SM sub-partition, so the fast phase is short.
-constexpr uint32_t kFastSpins = 16;
+// kFastSpins polls touch nothing else.  An isolated mbarrier round trip is
+// fastest with a long pure spin (228 vs 492 cycles on B200), but inside the
+// attention kernel spinning warps steal issue slots from the warps that share
+// their SM sub-partition; one poll before the timed loop measured fastest
+// there (1, 4, 16, 64 polls: 835, 806, 804, 787 TFLOP/s).
+constexpr uint32_t kFastSpins = 1;
 
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           int* status, int site, uint64_t timeout_ns) {
