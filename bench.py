@@ -408,7 +408,18 @@ def run_reference(args, wl: dict) -> dict:
             "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+def _json_out():
+    """The one JSON line goes to the original stdout; everything else written to
+    file descriptor 1 during the run (NCCL prints its version banner there) is
+    sent to stderr, so stdout carries exactly one line."""
+    saved = os.dup(1)
+    sys.stdout.flush()
+    os.dup2(2, 1)
+    return os.fdopen(saved, "w")
+
+
 def main():
+    out = _json_out()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
@@ -429,7 +440,7 @@ def main():
         rank = int(os.environ.get("RANK", "0"))
         if rank != 0:
             return 0
-        print(json.dumps(run_reference(args, wl)), flush=True)
+        print(json.dumps(run_reference(args, wl)), file=out, flush=True)
         return 0
 
     rank, world, local = dist_setup()
@@ -443,7 +454,7 @@ def main():
 
             dist.destroy_process_group()
     if res is not None:
-        print(json.dumps(res), flush=True)
+        print(json.dumps(res), file=out, flush=True)
     return 0
 
 
