@@ -64,60 +64,98 @@ __device__ __forceinline__ void store8(T* p, const float (&v)[8]) {
   }
 }
 
-// Eight threads per 64-wide row; thread g holds elements [8g, 8g+8).  The
-// RoPE partner of element i < 32 is i + 32, held by thread g ^ 4.
+constexpr int kPrepTokens = 32;     // tokens per block (8 threads per 64-wide row)
+constexpr int kPrepSeqPerBlock = 16;  // sequences (s, h) a block sweeps with one staged table slice
+
+// K' = RoPE(LN(x)) over (SH, T, 64).  A block owns kPrepTokens consecutive
+// tokens of up to kPrepSeqPerBlock sequences: the sin/cos rows of its tokens
+// are staged in shared memory once and reused for every sequence (the table
+// row depends on the token only), which keeps the table reads from costing
+// more L2 traffic than the rows themselves.  Eight threads per row; thread g
+// holds elements [8g, 8g+8) and the RoPE partner of element i < 32 (i + 32)
+// sits in thread g ^ 4.
 template <typename In, typename Out>
-__global__ void __launch_bounds__(256) qk_prep_kernel(const In* __restrict__ x, Out* __restrict__ out, uint64_t rows,
+__global__ void __launch_bounds__(256) qk_prep_kernel(const In* __restrict__ x, Out* __restrict__ out, uint32_t sh,
                                                       uint32_t t, QkPrologue p) {
-  const uint64_t gt = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const uint64_t row = gt >> 3;
-  const int g = static_cast<int>(gt & 7);
-  const bool valid = row < rows;
-  float v[8];
-  if (valid) {
-    load8(x + row * 64 + 8 * g, v);
-  } else {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = 0.f;
-  }
-  if (p.ln) {
-    float s = 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) s += v[i];
-    s += __shfl_xor_sync(0xffffffffu, s, 1);
-    s += __shfl_xor_sync(0xffffffffu, s, 2);
-    s += __shfl_xor_sync(0xffffffffu, s, 4);
-    const float mu = s * (1.0f / 64);
-    float q = 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float d = v[i] - mu;
-      q = fmaf(d, d, q);
-    }
-    q += __shfl_xor_sync(0xffffffffu, q, 1);
-    q += __shfl_xor_sync(0xffffffffu, q, 2);
-    q += __shfl_xor_sync(0xffffffffu, q, 4);
-    const float inv = rsqrtf(q * (1.0f / 64) + p.eps);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = (v[i] - mu) * inv * __ldg(p.ln_w + 8 * g + i) + __ldg(p.ln_b + 8 * g + i);
-  }
+  __shared__ float sin_s[kPrepTokens][64];
+  __shared__ float cos_s[kPrepTokens][64];
+  __shared__ int rot_s[kPrepTokens];
+  const int lt = threadIdx.x >> 3;  // token within the block
+  const int g = threadIdx.x & 7;
+  const uint32_t tok = blockIdx.x * kPrepTokens + lt;
+  const bool tok_ok = tok < t;
   if (p.rope) {
-    float pv[8];
+    if (threadIdx.x < kPrepTokens) {
+      const uint32_t tk = blockIdx.x * kPrepTokens + threadIdx.x;
+      const uint32_t ft = (tk + p.pos_offset) % p.tokens_per_frame;
+      rot_s[threadIdx.x] = (tk < t && ft >= p.prefix) ? static_cast<int>(ft - p.prefix) : -1;
+    }
+    __syncthreads();
+    // Scalar loads: the tables come through the C ABI with only 4-byte alignment promised.
+    for (int i = threadIdx.x; i < kPrepTokens * 64; i += blockDim.x) {
+      const int tt = i >> 6, c = i & 63;
+      const int r = rot_s[tt];
+      float sv = 0.f, cv = 1.f;
+      if (r >= 0) {
+        sv = __ldg(p.sin_t + static_cast<uint64_t>(r) * 64 + c);
+        cv = __ldg(p.cos_t + static_cast<uint64_t>(r) * 64 + c);
+      }
+      sin_s[tt][c] = sv;
+      cos_s[tt][c] = cv;
+    }
+    __syncthreads();
+  }
+  float w[8], bb[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) pv[i] = __shfl_xor_sync(0xffffffffu, v[i], 4);
-    const uint32_t tok = static_cast<uint32_t>(row % t);
-    const uint32_t ft = (tok + p.pos_offset) % p.tokens_per_frame;
-    if (valid && ft >= p.prefix) {
-      const uint64_t r = static_cast<uint64_t>(ft - p.prefix) * 64 + 8 * g;
+  for (int i = 0; i < 8; ++i) {
+    w[i] = p.ln ? __ldg(p.ln_w + 8 * g + i) : 1.f;
+    bb[i] = p.ln ? __ldg(p.ln_b + 8 * g + i) : 0.f;
+  }
+  const uint32_t seq_end = min(sh, (blockIdx.y + 1) * kPrepSeqPerBlock);
+  for (uint32_t q = blockIdx.y * kPrepSeqPerBlock; q < seq_end; ++q) {
+    const uint64_t row = static_cast<uint64_t>(q) * t + tok;
+    float v[8];
+    if (tok_ok) {
+      load8(x + row * 64 + 8 * g, v);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = 0.f;
+    }
+    if (p.ln) {
+      float sm = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) sm += v[i];
+      sm += __shfl_xor_sync(0xffffffffu, sm, 1);
+      sm += __shfl_xor_sync(0xffffffffu, sm, 2);
+      sm += __shfl_xor_sync(0xffffffffu, sm, 4);
+      const float mu = sm * (1.0f / 64);
+      float sq = 0.f;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const float sn = __ldg(p.sin_t + r + i), cs = __ldg(p.cos_t + r + i);
+        const float d = v[i] - mu;
+        sq = fmaf(d, d, sq);
+      }
+      sq += __shfl_xor_sync(0xffffffffu, sq, 1);
+      sq += __shfl_xor_sync(0xffffffffu, sq, 2);
+      sq += __shfl_xor_sync(0xffffffffu, sq, 4);
+      const float inv = rsqrtf(sq * (1.0f / 64) + p.eps);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = (v[i] - mu) * inv * w[i] + bb[i];
+    }
+    if (p.rope) {
+      float pv[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) pv[i] = __shfl_xor_sync(0xffffffffu, v[i], 4);
+      // Pass-through rows hold sin 0 / cos 1, so every row takes the same path.
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float sn = sin_s[lt][8 * g + i], cs = cos_s[lt][8 * g + i];
         // lower half: x*cos - x[i+32]*sin ; upper half: x*cos + x[i-32]*sin
         v[i] = g < 4 ? v[i] * cs - pv[i] * sn : v[i] * cs + pv[i] * sn;
       }
     }
+    if (tok_ok) store8(out + row * 64 + 8 * g, v);
   }
-  if (valid) store8(out + row * 64 + 8 * g, v);
 }
 
 // One warp per row, any width; two-pass statistics like layernorm.wesl.
@@ -200,16 +238,17 @@ inline unsigned blocks_for(uint64_t threads, unsigned per_block) {
 template <typename In>
 cudaError_t prep_dispatch_out(cudaStream_t stream, const In* x, void* out, int out_code, uint64_t rows, uint32_t t,
                               const QkPrologue& p) {
-  const unsigned grid = blocks_for(rows * 8, 256);
+  const uint32_t sh = static_cast<uint32_t>(rows / t);
+  const dim3 grid((t + kPrepTokens - 1) / kPrepTokens, (sh + kPrepSeqPerBlock - 1) / kPrepSeqPerBlock, 1);
   switch (out_code) {
     case kBF16:
-      qk_prep_kernel<In, __nv_bfloat16><<<grid, 256, 0, stream>>>(x, static_cast<__nv_bfloat16*>(out), rows, t, p);
+      qk_prep_kernel<In, __nv_bfloat16><<<grid, 256, 0, stream>>>(x, static_cast<__nv_bfloat16*>(out), sh, t, p);
       break;
     case kF16:
-      qk_prep_kernel<In, __half><<<grid, 256, 0, stream>>>(x, static_cast<__half*>(out), rows, t, p);
+      qk_prep_kernel<In, __half><<<grid, 256, 0, stream>>>(x, static_cast<__half*>(out), sh, t, p);
       break;
     default:
-      qk_prep_kernel<In, float><<<grid, 256, 0, stream>>>(x, static_cast<float*>(out), rows, t, p);
+      qk_prep_kernel<In, float><<<grid, 256, 0, stream>>>(x, static_cast<float*>(out), sh, t, p);
       break;
   }
   return cudaGetLastError();
