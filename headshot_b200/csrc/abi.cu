@@ -119,43 +119,40 @@ hs_status attention_impl(hs_ctx* ctx, const void* q, const void* k, const void* 
   const int elem = dtype == HS_F16 ? kF16 : kBF16;  // tensor-core operand type (f32 -> bf16)
   const uint64_t rows = static_cast<uint64_t>(S) * H * T;
   const size_t tile_bytes = rows * 64 * 2;
+  // Rows the attention kernel cannot take as given (f32 storage, or q/k that
+  // need the QK-norm/RoPE prologue) go through qk_prep into scratch first.
+  const bool q_direct = code != kF32 && !qp.ln && !qp.rope;
   const bool k_direct = code != kF32 && !kp.ln && !kp.rope;
   const bool v_direct = code != kF32;
-  size_t need = (k_direct ? 0 : tile_bytes) + (v_direct ? 0 : tile_bytes);
+  const size_t need = (q_direct ? 0 : tile_bytes) + (k_direct ? 0 : tile_bytes) + (v_direct ? 0 : tile_bytes);
   void* scratch = nullptr;
   if (need) {
     hs_status s = ctx_scratch(ctx, need, &scratch);
     if (s != HS_OK) return s;
   }
-  const void* k_use = k;
-  const void* v_use = v;
+  const void* use[3] = {q, k, v};
+  const bool direct[3] = {q_direct, k_direct, v_direct};
+  const QkPrologue none{};
+  const QkPrologue* pro[3] = {&qp, &kp, &none};
+  static const char* const what[3] = {"qk_prep(q)", "qk_prep(k)", "cast(v)"};
   uint8_t* cursor = static_cast<uint8_t*>(scratch);
   cudaError_t e;
-  if (!k_direct) {
+  for (int i = 0; i < 3; ++i) {
+    if (direct[i]) continue;
     {
       ProfScope prof(ctx, st, "qk_prep");
-      e = launch_qk_prep(st, k, code, cursor, elem, rows, T, kp);
+      e = launch_qk_prep(st, use[i], code, cursor, elem, rows, T, *pro[i]);
     }
-    if (e != cudaSuccess) return cuda_fail(e, "qk_prep(k)");
-    k_use = cursor;
+    if (e != cudaSuccess) return cuda_fail(e, what[i]);
+    use[i] = cursor;
     cursor += tile_bytes;
-  }
-  if (!v_direct) {
-    QkPrologue none{};
-    {
-      ProfScope prof(ctx, st, "qk_prep");
-      e = launch_qk_prep(st, v, code, cursor, elem, rows, T, none);
-    }
-    if (e != cudaSuccess) return cuda_fail(e, "cast(v)");
-    v_use = cursor;
   }
   std::string err;
   AttnState state{};
   {
     ProfScope prof(ctx, st, "attention");
-    e = launch_attention_sm100(st, elem, q, code == kF32 ? kF32 : elem, k_use, v_use, out,
-                               code == kF32 ? kF32 : elem, S * H, T, T, scale, qp, state, ctx->d_status,
-                               ctx_timeout_ns(ctx), &err);
+    e = launch_attention_sm100(st, elem, use[0], use[1], use[2], out, code == kF32 ? kF32 : elem, S * H, T, T,
+                               scale, state, 0, ctx->d_status, ctx->d_sched, ctx_timeout_ns(ctx), &err);
   }
   if (e != cudaSuccess) return fail(HS_ERR_CUDA, std::string(name) + ": " + (err.empty() ? cudaGetErrorString(e) : err));
   return HS_OK;
@@ -195,6 +192,7 @@ hs_status hs_ctx_create(int device, hs_ctx** out) {
   }
   e = cudaMalloc(&ctx->d_status, sizeof(int) * 4);
   if (e == cudaSuccess) e = cudaMemset(ctx->d_status, 0, sizeof(int) * 4);
+  ctx->d_sched = reinterpret_cast<uint32_t*>(ctx->d_status + 2);
   if (e != cudaSuccess) {
     cudaStreamDestroy(ctx->stream);
     delete ctx;

@@ -5,16 +5,32 @@
 // GpuContext::attention, src/engine/ops.rs:228-253) for the aggregator's
 // frame and global attention.  Same contract: q, k, v, out head-major
 // (S·H, T, 64); out = softmax(q·kᵀ·scale)·v with f32 softmax statistics.
+// q, k and v reach this kernel as 16-bit rows; the QK-norm + RoPE prologue
+// of the fused op has already been applied to q and k by qk_prep (ops.cu).
 //
-// One CTA owns 256 query rows of one (s, h) sequence as two 128-row tiles
-// and streams all 96-key K/V tiles of that sequence:
+// The kernel is persistent: one CTA per SM takes work items from a global
+// counter (the producer thread fetches the next index one item ahead and
+// hands it to the other warps through a small ring in shared memory).  An
+// item is 256 query rows of one (s, h) sequence, split into two 128-row
+// tiles, one per softmax warpgroup, against every 96-key K/V tile of that
+// sequence.  Items go out in sequence-major order, so the CTAs working at
+// one time share a few sequences' K/V in L2, and a CTA that runs ahead
+// simply takes more items (no tail from a fixed assignment).
 //
 //   warps 0-3   softmax warpgroup 0 (one thread per query row)
 //   warps 4-7   softmax warpgroup 1
-//   warp  8     TMA producer: K and V 96x64 tiles, 128B-swizzled, kStages ring
+//   warp  8     TMA producer: Q tiles (double-buffered per warpgroup) and
+//               K and V 96x64 tiles (kStages ring), all 128B-swizzled
 //   warp  9     UMMA issue for warpgroup 0 (whole warp; elect.sync issues)
 //   warp  10    UMMA issue for warpgroup 1
 //   warp  11    TMEM owner (alloc/free)
+//
+// The producer runs ahead across item boundaries, so the next item's Q and
+// first K/V tiles are already in shared memory when the MMA warps finish an
+// item; the MMA warps issue the next item's first score tiles while the
+// softmax warpgroups are still storing the previous output.  When an item's
+// second 128-row tile lies wholly past the sequence end, warpgroup 1 and its
+// MMA warp skip the item (the MMA warp only releases the K/V stages).
 //
 // TMEM (512 columns x 128 lanes): two score buffers per warpgroup,
 // S[wg][b] = columns (2*wg + b) * 96 .. +96 (f32), and the accumulators
@@ -34,11 +50,9 @@
 // the max grows by more than 2^8), evaluates the exponentials partly on
 // MUFU.EX2 and partly as a polynomial on the FMA pipe, works on packed
 // f32x2 pairs, and reads/writes TMEM with tcgen05.ld/st.
-//
-// The Q tile is loaded by the softmax threads themselves, one row per
-// thread, and goes through the fused QK-norm + RoPE prologue in f32 before
-// being written to shared memory in the UMMA 128B-swizzle layout.
 #include <cuda.h>
+
+#include <mutex>
 
 #include "hs_internal.h"
 #include "hs_ptx.cuh"
@@ -48,9 +62,13 @@ namespace {
 
 constexpr int kD = 64;
 constexpr int kBM = 128;  // query rows per tile / softmax warpgroup
+constexpr int kItemRows = 2 * kBM;
 constexpr int kBN = 96;   // keys per KV tile: 4 score buffers x 96 + 2 accumulators x 64 = 512 TMEM columns
 constexpr int kPairs = kBN / 2;
 constexpr int kStages = 6;
+constexpr int kQBufs = 2;                   // Q tiles per warpgroup: the current item's and the next one's
+constexpr int kItemSlots = 4;               // item indices handed from the producer to the other warps
+constexpr int kItemReaders = 8 + 2;         // one arrival per softmax warp and per MMA warp
 constexpr int kQTileBytes = kBM * kD * 2;   // 16 KiB
 constexpr int kKvTileBytes = kBN * kD * 2;  // 12 KiB
 constexpr int kThreads = 384;  // 3 warpgroups: softmax 0, softmax 1, control
@@ -72,47 +90,80 @@ constexpr int kEmuPer8 = 1;                // of every 8 exponential pairs, this
 enum : int {
   kSiteQFull = 0x101,
   kSiteKvFull = 0x102,
+  kSiteQEmpty = 0x103,
   kSitePFull = 0x104,
   kSiteSFull = 0x105,
   kSiteODone = 0x106,
   kSiteKvEmpty = 0x107,
+  kSiteItemFull = 0x108,
+  kSiteItemEmpty = 0x109,
 };
 
-// Every per-tile barrier is doubled by tile parity so no waiter can fall two
-// phases behind (parity waits cannot tell phase n from phase n+2).
+// Barrier phases are counted per barrier across all items of a CTA; every
+// waiter knows how many completions precede the one it wants.  Parity waits
+// cannot tell phase n from phase n+2, so each barrier is arranged such that
+// its next completion needs an action of the waiter taken after the wait:
+// S buffers are doubled by tile parity, PV-only batches at the end of an
+// item complete pv_done instead of an S buffer, Q buffers are doubled.
 struct Ctrl {
-  uint64_t kv_full[kStages];   // K and V tile of a stage landed (one transaction count)
-  uint64_t kv_empty[kStages];  // both MMA warps are done with the stage
-  uint64_t q_full[2];          // Q tile of a warpgroup is in shared memory
-  uint64_t s_full[2][2];       // [wg][buf]: S(j) landed; next phase: PV(j) and S(j+2) landed
-  uint64_t p_full[2][2];       // softmax wrote P (and rescaled O) for the tile in that buffer
-  uint64_t drain[2];           // every MMA of that warpgroup's MMA warp completed
+  uint64_t kv_full[kStages];      // K and V tile of a stage landed (one transaction count)
+  uint64_t kv_empty[kStages];     // both MMA warps are done with the stage
+  uint64_t q_full[2][kQBufs];     // [wg][buf] Q tile landed
+  uint64_t q_empty[2][kQBufs];    // the item's last QKᵀ product using that Q tile completed
+  uint64_t s_full[2][2];          // [wg][buf]: S(j) landed (with PV(j-2) before it)
+  uint64_t p_full[2][2];          // softmax wrote P (and rescaled O) for the tile in that buffer
+  uint64_t pv_done[2];            // a PV product with no S behind it (the last two of an item) completed
+  uint64_t drain[2];              // every MMA of that warpgroup's MMA warp completed
+  uint64_t item_full[kItemSlots];   // the producer wrote an item index into the slot
+  uint64_t item_empty[kItemSlots];  // every reader took it
+  uint32_t item_slot[kItemSlots];   // item index; >= n_items means no more work
   uint32_t tmem_base;
   int abort_flag;
-  float ln_w[kD];
-  float ln_b[kD];
 };
 
 constexpr size_t kSmemBytes =
-    1024 /*alignment slack*/ + 2 * kQTileBytes + 2 * kStages * kKvTileBytes + sizeof(Ctrl);
+    1024 /*alignment slack*/ + 2 * kQBufs * kQTileBytes + 2 * kStages * kKvTileBytes + sizeof(Ctrl);
 static_assert(kKvTileBytes % 1024 == 0, "swizzle atoms of each stage must stay 1024-byte aligned");
+static_assert(kSmemBytes <= 232448, "shared memory per CTA");
 
 struct Args {
-  const void* q;
   void* out;
-  uint32_t t_q;   // query rows per sequence
-  uint32_t t_kv;  // keys per sequence
-  uint32_t n_kv;  // ceil(t_kv / kBN)
-  int q_f32;
+  uint32_t t_q;      // query rows per sequence
+  uint32_t t_kv;     // keys per sequence
+  uint32_t n_kv;     // ceil(t_kv / kBN)
+  uint32_t pairs;    // items per sequence: ceil(t_q / 256)
+  uint32_t n_items;  // sequences x pairs
   int out_f32;
   float scale_log2;
-  QkPrologue qp;
   AttnState st;
   int* status;
+  uint32_t* sched;  // [0] items handed out beyond the first gridDim.x, [1] CTAs finished
   uint64_t timeout_ns;
 };
 
+struct Item {
+  uint32_t seq;
+  uint32_t row0;  // first query row of the item
+};
+
+__device__ __forceinline__ Item decode_item(const Args& a, uint32_t item) {
+  const uint32_t seq = item / a.pairs;
+  return Item{seq, (item - seq * a.pairs) * kItemRows};
+}
+
 __device__ __forceinline__ float u2f(uint32_t u) { return __uint_as_float(u); }
+
+// Position in the K/V stage ring: stage index and the parity of its use count.
+struct RingPos {
+  uint32_t stage = 0;
+  uint32_t phase = 0;
+  __device__ __forceinline__ void next() {
+    if (++stage == kStages) {
+      stage = 0;
+      phase ^= 1;
+    }
+  }
+};
 
 // Bounded wait whose outcome is the same for all 32 lanes, so the
 // .sync.aligned tcgen05 instructions that follow never see a split warp.
@@ -122,77 +173,27 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
   return __all_sync(0xffffffffu, r);
 }
 
-// Loads one 64-wide query row (16-bit or f32 storage) into f32 registers.
-template <typename E>
-__device__ __forceinline__ void load_row(const Args& a, uint64_t row_index, float (&x)[kD]) {
-  if (a.q_f32) {
-    const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(a.q) + row_index * kD);
-#pragma unroll
-    for (int c = 0; c < kD / 4; ++c) {
-      float4 v = __ldg(src + c);
-      x[4 * c + 0] = v.x;
-      x[4 * c + 1] = v.y;
-      x[4 * c + 2] = v.z;
-      x[4 * c + 3] = v.w;
-    }
-  } else {
-    const uint4* src = reinterpret_cast<const uint4*>(static_cast<const E*>(a.q) + row_index * kD);
-#pragma unroll
-    for (int c = 0; c < kD / 8; ++c) {
-      uint4 v = __ldg(src + c);
-      float2 f0 = Elem<E>::unpack2(v.x), f1 = Elem<E>::unpack2(v.y);
-      float2 f2 = Elem<E>::unpack2(v.z), f3 = Elem<E>::unpack2(v.w);
-      x[8 * c + 0] = f0.x;
-      x[8 * c + 1] = f0.y;
-      x[8 * c + 2] = f1.x;
-      x[8 * c + 3] = f1.y;
-      x[8 * c + 4] = f2.x;
-      x[8 * c + 5] = f2.y;
-      x[8 * c + 6] = f3.x;
-      x[8 * c + 7] = f3.y;
-    }
-  }
+// Next item index for a reader warp (all lanes): waits for slot k % kItemSlots,
+// reads it, and releases the slot with one arrival per warp.  Returns false
+// on timeout/abort.
+__device__ __forceinline__ bool next_item(const Args& a, Ctrl* ctl, uint32_t k, uint32_t* item) {
+  const uint32_t slot = k % kItemSlots;
+  if (!warp_wait(&ctl->item_full[slot], (k / kItemSlots) & 1, &ctl->abort_flag, a.status, kSiteItemFull,
+                 a.timeout_ns))
+    return false;
+  *item = *reinterpret_cast<volatile uint32_t*>(&ctl->item_slot[slot]);
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(&ctl->item_empty[slot]);
+  return true;
 }
 
-// QK-norm (two-pass mean/variance in f32) then rotate-half RoPE on one row.
-__device__ __forceinline__ void prologue_row(const Args& a, const Ctrl* ctl, uint32_t token, float (&x)[kD]) {
-  if (a.qp.ln) {
-    float s = 0.f;
-#pragma unroll
-    for (int i = 0; i < kD; ++i) s += x[i];
-    const float mu = s * (1.0f / kD);
-    float v = 0.f;
-#pragma unroll
-    for (int i = 0; i < kD; ++i) {
-      const float d = x[i] - mu;
-      v = fmaf(d, d, v);
-    }
-    const float inv = rsqrtf(v * (1.0f / kD) + a.qp.eps);
-#pragma unroll
-    for (int i = 0; i < kD; ++i) x[i] = (x[i] - mu) * inv * ctl->ln_w[i] + ctl->ln_b[i];
-  }
-  if (a.qp.rope) {
-    const uint32_t ft = (token + a.qp.pos_offset) % a.qp.tokens_per_frame;
-    if (ft >= a.qp.prefix) {
-      const uint64_t r = static_cast<uint64_t>(ft - a.qp.prefix) * kD;
-      const float4* sn = reinterpret_cast<const float4*>(a.qp.sin_t + r);
-      const float4* cs = reinterpret_cast<const float4*>(a.qp.cos_t + r);
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {  // pairs (i, i+32), 4 at a time
-        const float4 sl = __ldg(sn + c), sh = __ldg(sn + 8 + c);
-        const float4 cl = __ldg(cs + c), ch = __ldg(cs + 8 + c);
-        const float sl_[4] = {sl.x, sl.y, sl.z, sl.w}, sh_[4] = {sh.x, sh.y, sh.z, sh.w};
-        const float cl_[4] = {cl.x, cl.y, cl.z, cl.w}, ch_[4] = {ch.x, ch.y, ch.z, ch.w};
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int i = 4 * c + u;
-          const float lo = x[i], hi = x[i + 32];
-          x[i] = lo * cl_[u] - hi * sl_[u];
-          x[i + 32] = hi * ch_[u] + lo * sh_[u];
-        }
-      }
-    }
-  }
+// One arrival from a converged warp (the elected lane).
+__device__ __forceinline__ void mbar_arrive_elect(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t.reg .b32 r;\n\t"
+      "elect.sync r|e, 0xffffffff;\n\t"
+      "@e mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];\n\t}" ::"r"(smem_u32(bar))
+      : "memory");
 }
 
 // ---- packed f32x2 arithmetic (sm_100) and the FMA-pipe exp2 -------------
@@ -249,232 +250,261 @@ __device__ __forceinline__ void exp2_poly2(float x0, float x1, float& y0, float&
 }
 
 template <typename E>
-__device__ void softmax_role(const Args& a, uint8_t* sQ, Ctrl* ctl, uint32_t tmem, int warp, int lane) {
+__device__ void softmax_role(const Args& a, Ctrl* ctl, uint32_t tmem, int warp, int lane) {
   const int wg = warp >> 2;
   const int wq = warp & 3;
   const uint32_t row = static_cast<uint32_t>(wq * 32 + lane);
-  const uint32_t token = blockIdx.x * (2 * kBM) + wg * kBM + row;
-  const bool valid = token < a.t_q;
-  const uint64_t row_index = static_cast<uint64_t>(blockIdx.y) * a.t_q + token;
   volatile int* abort_flag = &ctl->abort_flag;
-
-  // ---- Q prologue: global -> f32 -> QK-norm/RoPE -> swizzled smem --------
-  {
-    float x[kD];
-    if (valid) {
-      load_row<E>(a, row_index, x);
-      prologue_row(a, ctl, token, x);
-    } else {
-#pragma unroll
-      for (int i = 0; i < kD; ++i) x[i] = 0.f;
-    }
-    uint8_t* dst = sQ + wg * kQTileBytes + row * 128;
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      uint4 v;
-      v.x = Elem<E>::pack2(x[8 * c + 0], x[8 * c + 1]);
-      v.y = Elem<E>::pack2(x[8 * c + 2], x[8 * c + 3]);
-      v.z = Elem<E>::pack2(x[8 * c + 4], x[8 * c + 5]);
-      v.w = Elem<E>::pack2(x[8 * c + 6], x[8 * c + 7]);
-      *reinterpret_cast<uint4*>(dst + ((c ^ (row & 7)) << 4)) = v;
-    }
-    fence_proxy_async_smem();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&ctl->q_full[wg]);  // one arrival per warp
-  }
-
   const uint32_t lane_base = static_cast<uint32_t>(wq * 32) << 16;
   const uint32_t tO = tmem + lane_base + col_o(wg);
   const float c = a.scale_log2;
-  const uint32_t tail = a.t_kv - (a.n_kv - 1) * kBN;  // valid keys in the last tile, 1..kBN
+  const uint32_t n = a.n_kv;
+  const uint32_t tail = a.t_kv - (n - 1) * kBN;  // valid keys in the last tile, 1..kBN
+  // Completions per item: s_full[b] once per S tile with j % 2 == b,
+  // pv_done once per PV-only batch (the last min(n, 2) tiles).
+  // Only the parities of the completion counts before an item matter; they
+  // are packed into one register: bit 0 s_full[0], bit 1 s_full[1], bit 2
+  // pv_done.  Per item the counts grow by ceil(n/2), floor(n/2), min(n, 2).
+  const uint32_t step_bits = (((n + 1) >> 1) & 1) | (((n >> 1) & 1) << 1);  // pv_done grows by an even count
+  const uint32_t pv_last = n >= 2 ? 1 : 0;  // the epilogue waits the item's pv_done completion 1 + pv_last
+  uint32_t base_bits = 0;
+  auto s_parity = [&](uint32_t t) { return ((base_bits >> (t & 1)) + (t >> 1)) & 1; };
 
-  float m_run = -INFINITY, l = 0.f;
-  bool have_o = false;
-  if (a.st.load && valid) {
-    m_run = a.st.m[row_index];
-    l = a.st.l[row_index];
-  }
-  if (a.st.load) {
-    // Seed O in TMEM with the carried accumulator (zeros for padding rows).
-    uint32_t o[32];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const float4* src = reinterpret_cast<const float4*>(a.st.o + row_index * kD + 32 * h);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        float4 v = valid ? src[i] : make_float4(0.f, 0.f, 0.f, 0.f);
-        o[4 * i + 0] = __float_as_uint(v.x);
-        o[4 * i + 1] = __float_as_uint(v.y);
-        o[4 * i + 2] = __float_as_uint(v.z);
-        o[4 * i + 3] = __float_as_uint(v.w);
-      }
-      tmem_st32(tO + 32 * h, o);
-    }
-    tmem_wait_st();
-    have_o = true;
-    if (!valid) m_run = 0.f;
-  }
+  for (uint32_t k = 0;; ++k) {
+    uint32_t item;
+    if (!next_item(a, ctl, k, &item)) return;
+    if (item >= a.n_items) break;
+    const Item it = decode_item(a, item);
+    const uint32_t tile0 = it.row0 + wg * kBM;
+    if (tile0 >= a.t_q) continue;  // this warpgroup has no rows in the item
+    const uint32_t token = tile0 + row;
+    const bool valid = token < a.t_q;
+    const uint64_t row_index = static_cast<uint64_t>(it.seq) * a.t_q + token;
 
-  bool ok = true;
-  for (uint32_t j = 0; j < a.n_kv; ++j) {
-    const int b = static_cast<int>(j & 1);
-    if (!warp_wait(&ctl->s_full[wg][b], (j >> 1) & 1, abort_flag, a.status, kSiteSFull, a.timeout_ns)) {
-      ok = false;
-      break;
+    float m_run = -INFINITY, l = 0.f;
+    bool have_o = false;
+    if (a.st.load && valid) {
+      m_run = a.st.m[row_index];
+      l = a.st.l[row_index];
     }
-    tc_fence_after();
-    const uint32_t tS = tmem + lane_base + col_s(wg, b);
-    uint32_t s[kBN];
-    tmem_ld32(tS + 0, s + 0);
-    tmem_ld32(tS + 32, s + 32);
-    tmem_ld32(tS + 64, s + 64);
-    tmem_wait_ld_regs<kBN>(s);
-    if (j == a.n_kv - 1 && tail < kBN) {
-#pragma unroll
-      for (int i = 0; i < kBN; ++i)
-        if (static_cast<uint32_t>(i) >= tail) s[i] = __float_as_uint(-INFINITY);
-    }
-    // Row max: 3-input max in four independent chains.
-    float m4[4] = {u2f(s[0]), u2f(s[1]), u2f(s[2]), u2f(s[3])};
-#pragma unroll
-    for (int i = 4; i < kBN; i += 2) m4[(i >> 1) & 3] = max3(m4[(i >> 1) & 3], u2f(s[i]), u2f(s[i + 1]));
-    const float m_tile = max3(fmaxf(m4[0], m4[1]), m4[2], m4[3]) * c;
-
-    float factor = 1.f;
-    bool need = false;
-    if (!have_o) {
-      m_run = m_tile;
-    } else if (m_tile > m_run + kRescaleThreshold) {
-      factor = ex2_approx(m_run - m_tile);
-      m_run = m_tile;
-      l *= factor;
-      need = true;
-    }
-    // P = 2^(s*c - m) on packed f32x2 pairs; kEmuPer8 of every 8 pairs take
-    // the FMA-pipe exp2, the rest MUFU.EX2.  P overwrites the first kPairs
-    // columns of this S buffer (already read into registers).  The row sum
-    // adds the rounded 16-bit P the tensor core multiplies (mixed-precision
-    // add into f32), so the rounding of dominant weights cancels in O / l.
-    const float neg_m = -m_run;
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    uint32_t pk[kPairs];
-#pragma unroll
-    for (int i = 0; i < kPairs; ++i) {
-      float x0, x1, p0, p1;
-      fma2(x0, x1, u2f(s[2 * i]), u2f(s[2 * i + 1]), c, c, neg_m, neg_m);
-      if ((i & 7) < kEmuPer8) {
-        exp2_poly2(x0, x1, p0, p1);
-      } else {
-        p0 = ex2_approx(x0);
-        p1 = ex2_approx(x1);
-      }
-      pk[i] = Elem<E>::pack2(p0, p1);
-      Elem<E>::acc2(acc[2 * (i & 1)], acc[2 * (i & 1) + 1], pk[i]);
-      if (i == 31) tmem_st32(tS, pk);
-    }
-    tmem_st16(tS + 32, pk + 32);
-    l += (acc[0] + acc[1]) + (acc[2] + acc[3]);
-    // O rescale (rare), once the previous PV product has landed (the commit
-    // after PV(j-1) completes the next phase of the other buffer's s_full).
-    // PV(j) is issued only after p_full, so it accumulates onto the rescaled O.
-    if (__any_sync(0xffffffffu, need)) {
-      if (j > 0) {
-        if (!warp_wait(&ctl->s_full[wg][(j - 1) & 1], ((j + 1) >> 1) & 1, abort_flag, a.status, kSiteODone,
-                       a.timeout_ns)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-      }
+    if (a.st.load) {
+      // Seed O in TMEM with the carried accumulator (zeros for padding rows).
+      // The previous item's epilogue finished reading O (tcgen05.wait::ld).
+      uint32_t o[32];
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        uint32_t o[32];
-        tmem_ld32(tO + 32 * h, o);
-        tmem_wait_ld_regs<32>(o);
+        const float4* src = reinterpret_cast<const float4*>(a.st.o + row_index * kD + 32 * h);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(u2f(o[i]) * factor);
+        for (int i = 0; i < 8; ++i) {
+          float4 v = valid ? src[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+          o[4 * i + 0] = __float_as_uint(v.x);
+          o[4 * i + 1] = __float_as_uint(v.y);
+          o[4 * i + 2] = __float_as_uint(v.z);
+          o[4 * i + 3] = __float_as_uint(v.w);
+        }
         tmem_st32(tO + 32 * h, o);
       }
+      tmem_wait_st();
+      have_o = true;
+      if (!valid) m_run = 0.f;
     }
-    have_o = true;
-    tmem_wait_st();
-    tc_fence_before();
-    // One arrival per warp: 128 single-thread arrivals on one barrier word
-    // would serialise on the shared-memory atomic unit every tile.
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&ctl->p_full[wg][b]);
-  }
 
-  if (!ok) return;
-  // The commit after PV(n-1) is the next phase of the last tile's buffer.
-  const uint32_t last = a.n_kv - 1;
-  if (!warp_wait(&ctl->s_full[wg][last & 1], ((last + 2) >> 1) & 1, abort_flag, a.status, kSiteODone,
-                 a.timeout_ns))
-    return;
-  tc_fence_after();
+    for (uint32_t j = 0; j < n; ++j) {
+      const int b = static_cast<int>(j & 1);
+      if (!warp_wait(&ctl->s_full[wg][b], s_parity(j), abort_flag, a.status, kSiteSFull, a.timeout_ns)) return;
+      tc_fence_after();
+      const uint32_t tS = tmem + lane_base + col_s(wg, b);
+      uint32_t s[kBN];
+      tmem_ld32(tS + 0, s + 0);
+      tmem_ld32(tS + 32, s + 32);
+      tmem_ld32(tS + 64, s + 64);
+      tmem_wait_ld_regs<kBN>(s);
+      if (j == n - 1 && tail < kBN) {
+#pragma unroll
+        for (int i = 0; i < kBN; ++i)
+          if (static_cast<uint32_t>(i) >= tail) s[i] = __float_as_uint(-INFINITY);
+      }
+      // Row max: 3-input max in four independent chains.
+      float m4[4] = {u2f(s[0]), u2f(s[1]), u2f(s[2]), u2f(s[3])};
+#pragma unroll
+      for (int i = 4; i < kBN; i += 2) m4[(i >> 1) & 3] = max3(m4[(i >> 1) & 3], u2f(s[i]), u2f(s[i + 1]));
+      const float m_tile = max3(fmaxf(m4[0], m4[1]), m4[2], m4[3]) * c;
 
-  // ---- epilogue: O row from TMEM, normalise (or store the running state) --
+      float factor = 1.f;
+      bool need = false;
+      if (!have_o) {
+        m_run = m_tile;
+      } else if (m_tile > m_run + kRescaleThreshold) {
+        factor = ex2_approx(m_run - m_tile);
+        m_run = m_tile;
+        l *= factor;
+        need = true;
+      }
+      // P = 2^(s*c - m) on packed f32x2 pairs; kEmuPer8 of every 8 pairs take
+      // the FMA-pipe exp2, the rest MUFU.EX2.  P overwrites the first kPairs
+      // columns of this S buffer (already read into registers).  The row sum
+      // adds the rounded 16-bit P the tensor core multiplies (mixed-precision
+      // add into f32), so the rounding of dominant weights cancels in O / l.
+      const float neg_m = -m_run;
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      uint32_t pk[kPairs];
 #pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    uint32_t o[32];
-    tmem_ld32(tO + 32 * h, o);
-    tmem_wait_ld_regs<32>(o);
-    if (!valid) continue;
-    if (a.st.store) {
-      float4* dst = reinterpret_cast<float4*>(a.st.o + row_index * kD + 32 * h);
+      for (int i = 0; i < kPairs; ++i) {
+        float x0, x1, p0, p1;
+        fma2(x0, x1, u2f(s[2 * i]), u2f(s[2 * i + 1]), c, c, neg_m, neg_m);
+        if ((i & 7) < kEmuPer8) {
+          exp2_poly2(x0, x1, p0, p1);
+        } else {
+          p0 = ex2_approx(x0);
+          p1 = ex2_approx(x1);
+        }
+        pk[i] = Elem<E>::pack2(p0, p1);
+        Elem<E>::acc2(acc[2 * (i & 1)], acc[2 * (i & 1) + 1], pk[i]);
+        if (i == 31) tmem_st32(tS, pk);
+      }
+      tmem_st16(tS + 32, pk + 32);
+      l += (acc[0] + acc[1]) + (acc[2] + acc[3]);
+      // O rescale (rare), once PV(j-1) has landed.  PV(j-1) was committed
+      // together with S(j+1) when that tile exists, else (j = n-1) as the
+      // item's first PV-only batch.  PV(j) is issued only after p_full, so it
+      // accumulates onto the rescaled O.
+      if (__any_sync(0xffffffffu, need)) {
+        if (j > 0) {
+          const bool ok = (j + 1 < n) ? warp_wait(&ctl->s_full[wg][(j + 1) & 1], s_parity(j + 1), abort_flag,
+                                                  a.status, kSiteODone, a.timeout_ns)
+                                      : warp_wait(&ctl->pv_done[wg], (base_bits >> 2) & 1, abort_flag,
+                                                  a.status, kSiteODone, a.timeout_ns);
+          if (!ok) return;
+          tc_fence_after();
+        }
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
-        dst[i] = make_float4(u2f(o[4 * i]), u2f(o[4 * i + 1]), u2f(o[4 * i + 2]), u2f(o[4 * i + 3]));
-    } else {
-      const float inv_l = 1.0f / l;
-      if (a.out_f32) {
-        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + row_index * kD + 32 * h);
+        for (int h = 0; h < 2; ++h) {
+          uint32_t o[32];
+          tmem_ld32(tO + 32 * h, o);
+          tmem_wait_ld_regs<32>(o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(u2f(o[i]) * factor);
+          tmem_st32(tO + 32 * h, o);
+        }
+      }
+      have_o = true;
+      tmem_wait_st();
+      tc_fence_before();
+      // One arrival per warp: 128 single-thread arrivals on one barrier word
+      // would serialise on the shared-memory atomic unit every tile.
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ctl->p_full[wg][b]);
+    }
+
+    // PV(n-1) is the item's last PV-only batch.
+    if (!warp_wait(&ctl->pv_done[wg], ((base_bits >> 2) + pv_last) & 1, abort_flag, a.status, kSiteODone,
+                   a.timeout_ns))
+      return;
+    tc_fence_after();
+    base_bits ^= step_bits | (pv_last ? 0u : 4u);
+
+    // ---- epilogue: O row from TMEM, normalise (or store the running state) --
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint32_t o[32];
+      tmem_ld32(tO + 32 * h, o);
+      tmem_wait_ld_regs<32>(o);
+      if (!valid) continue;
+      if (a.st.store) {
+        float4* dst = reinterpret_cast<float4*>(a.st.o + row_index * kD + 32 * h);
 #pragma unroll
         for (int i = 0; i < 8; ++i)
-          dst[i] = make_float4(u2f(o[4 * i]) * inv_l, u2f(o[4 * i + 1]) * inv_l, u2f(o[4 * i + 2]) * inv_l,
-                               u2f(o[4 * i + 3]) * inv_l);
+          dst[i] = make_float4(u2f(o[4 * i]), u2f(o[4 * i + 1]), u2f(o[4 * i + 2]), u2f(o[4 * i + 3]));
       } else {
-        uint4* dst = reinterpret_cast<uint4*>(static_cast<E*>(a.out) + row_index * kD + 32 * h);
+        const float inv_l = 1.0f / l;
+        if (a.out_f32) {
+          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + row_index * kD + 32 * h);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          uint4 v;
-          v.x = Elem<E>::pack2(u2f(o[8 * i + 0]) * inv_l, u2f(o[8 * i + 1]) * inv_l);
-          v.y = Elem<E>::pack2(u2f(o[8 * i + 2]) * inv_l, u2f(o[8 * i + 3]) * inv_l);
-          v.z = Elem<E>::pack2(u2f(o[8 * i + 4]) * inv_l, u2f(o[8 * i + 5]) * inv_l);
-          v.w = Elem<E>::pack2(u2f(o[8 * i + 6]) * inv_l, u2f(o[8 * i + 7]) * inv_l);
-          dst[i] = v;
+          for (int i = 0; i < 8; ++i)
+            dst[i] = make_float4(u2f(o[4 * i]) * inv_l, u2f(o[4 * i + 1]) * inv_l, u2f(o[4 * i + 2]) * inv_l,
+                                 u2f(o[4 * i + 3]) * inv_l);
+        } else {
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<E*>(a.out) + row_index * kD + 32 * h);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            uint4 v;
+            v.x = Elem<E>::pack2(u2f(o[8 * i + 0]) * inv_l, u2f(o[8 * i + 1]) * inv_l);
+            v.y = Elem<E>::pack2(u2f(o[8 * i + 2]) * inv_l, u2f(o[8 * i + 3]) * inv_l);
+            v.z = Elem<E>::pack2(u2f(o[8 * i + 4]) * inv_l, u2f(o[8 * i + 5]) * inv_l);
+            v.w = Elem<E>::pack2(u2f(o[8 * i + 6]) * inv_l, u2f(o[8 * i + 7]) * inv_l);
+            dst[i] = v;
+          }
         }
       }
     }
-  }
-  if (valid && a.st.store) {
-    a.st.m[row_index] = m_run;
-    a.st.l[row_index] = l;
+    if (valid && a.st.store) {
+      a.st.m[row_index] = m_run;
+      a.st.l[row_index] = l;
+    }
   }
 }
 
-__device__ void producer_role(const Args& a, const CUtensorMap* tm_k, const CUtensorMap* tm_v, uint8_t* sK,
-                              uint8_t* sV, Ctrl* ctl) {
+// One thread.  Per item: the Q tiles of the warpgroups with rows in it, then
+// the item's K/V tiles through the stage ring.
+__device__ void producer_role(const Args& a, const CUtensorMap* tm_q, const CUtensorMap* tm_k,
+                              const CUtensorMap* tm_v, uint8_t* sQ, uint8_t* sK, uint8_t* sV, Ctrl* ctl) {
   volatile int* abort_flag = &ctl->abort_flag;
-  const int seq = static_cast<int>(blockIdx.y);
-  uint32_t issued = 0;
-  for (uint32_t j = 0; j < a.n_kv; ++j) {
-    const uint32_t st = j % kStages;
-    if (j >= kStages) {
-      if (!mbar_wait(&ctl->kv_empty[st], ((j / kStages) - 1) & 1, abort_flag, a.status, kSiteKvEmpty,
-                     a.timeout_ns))
-        break;
+  uint32_t q_issued[2] = {0, 0};
+  uint32_t g = 0;  // K/V tiles issued so far
+  bool ok = true;
+  uint32_t item = blockIdx.x;  // a CTA's first item is its index; later ones come from the counter
+  for (uint32_t k = 0; ok; ++k) {
+    const uint32_t slot = k % kItemSlots;
+    if (k >= kItemSlots && !mbar_wait(&ctl->item_empty[slot], ((k / kItemSlots) - 1) & 1, abort_flag, a.status,
+                                      kSiteItemEmpty, a.timeout_ns))
+      break;
+    ctl->item_slot[slot] = item;
+    mbar_arrive(&ctl->item_full[slot]);  // release: the index is visible to the readers' acquire
+    if (item >= a.n_items) break;
+    const Item it = decode_item(a, item);
+    item = gridDim.x + atomicAdd(a.sched, 1u);  // used one item later: the latency hides behind the loads
+#pragma unroll
+    for (int wg = 0; wg < 2; ++wg) {
+      const uint32_t tile0 = it.row0 + wg * kBM;
+      if (!ok || tile0 >= a.t_q) continue;
+      const uint32_t qi = q_issued[wg];
+      const uint32_t qb = qi % kQBufs;
+      if (qi >= kQBufs && !mbar_wait(&ctl->q_empty[wg][qb], ((qi / kQBufs) - 1) & 1, abort_flag, a.status,
+                                     kSiteQEmpty, a.timeout_ns)) {
+        ok = false;
+        continue;
+      }
+      mbar_arrive_expect_tx(&ctl->q_full[wg][qb], kQTileBytes);
+      tma_load_3d(tm_q, &ctl->q_full[wg][qb], sQ + (wg * kQBufs + qb) * kQTileBytes, 0, static_cast<int>(tile0),
+                  static_cast<int>(it.seq));
+      q_issued[wg] = qi + 1;
     }
-    mbar_arrive_expect_tx(&ctl->kv_full[st], 2 * kKvTileBytes);
-    tma_load_3d(tm_k, &ctl->kv_full[st], sK + st * kKvTileBytes, 0, static_cast<int>(j * kBN), seq);
-    tma_load_3d(tm_v, &ctl->kv_full[st], sV + st * kKvTileBytes, 0, static_cast<int>(j * kBN), seq);
-    issued = j + 1;
+    for (uint32_t j = 0; ok && j < a.n_kv; ++j, ++g) {
+      const uint32_t st = g % kStages;
+      if (g >= kStages &&
+          !mbar_wait(&ctl->kv_empty[st], ((g / kStages) - 1) & 1, abort_flag, a.status, kSiteKvEmpty,
+                     a.timeout_ns)) {
+        ok = false;
+        break;
+      }
+      mbar_arrive_expect_tx(&ctl->kv_full[st], 2 * kKvTileBytes);
+      tma_load_3d(tm_k, &ctl->kv_full[st], sK + st * kKvTileBytes, 0, static_cast<int>(j * kBN),
+                  static_cast<int>(it.seq));
+      tma_load_3d(tm_v, &ctl->kv_full[st], sV + st * kKvTileBytes, 0, static_cast<int>(j * kBN),
+                  static_cast<int>(it.seq));
+    }
   }
-  // Let every load this warp issued land before the CTA can exit.
-  const uint32_t first = issued > kStages ? issued - kStages : 0;
-  for (uint32_t j = first; j < issued; ++j) {
-    int no_abort = 0;
-    mbar_wait(&ctl->kv_full[j % kStages], (j / kStages) & 1, &no_abort, a.status, kSiteKvFull, a.timeout_ns);
+  // Let every load this thread issued land before the CTA can exit (on the
+  // normal path they have all been consumed already).
+  int no_abort = 0;
+  const uint32_t first = g > kStages ? g - kStages : 0;
+  for (uint32_t t = first; t < g; ++t)
+    mbar_wait(&ctl->kv_full[t % kStages], (t / kStages) & 1, &no_abort, a.status, kSiteKvFull, a.timeout_ns);
+#pragma unroll
+  for (int wg = 0; wg < 2; ++wg) {
+    const uint32_t qi = q_issued[wg];
+    for (uint32_t t = qi > kQBufs ? qi - kQBufs : 0; t < qi; ++t)
+      mbar_wait(&ctl->q_full[wg][t % kQBufs], (t / kQBufs) & 1, &no_abort, a.status, kSiteQFull, a.timeout_ns);
   }
 }
 
@@ -488,14 +518,22 @@ __device__ void mma_role(const Args& a, int wg, uint8_t* sQ, uint8_t* sK, uint8_
   constexpr uint32_t idesc_pv = idesc_f16(kBf16, kBM, kD, false, true);
   // Descriptor bases; a K=16 step of S advances the start field by
   // 32 B >> 4 = 2, a 16-key step of V by 2048 B >> 4 = 128.
-  const uint64_t q_desc = sdesc_sw128(smem_u32(sQ + wg * kQTileBytes), 16, 1024);
+  const uint64_t q_desc0 = sdesc_sw128(smem_u32(sQ + wg * kQBufs * kQTileBytes), 16, 1024);
   const uint64_t k_desc = sdesc_sw128(smem_u32(sK), 16, 1024);
   const uint64_t v_desc = sdesc_sw128(smem_u32(sV), 16, 1024);
   constexpr uint64_t kKvTileStep = kKvTileBytes >> 4;
+  constexpr uint64_t kQTileStep = kQTileBytes >> 4;
   const uint32_t o_tmem = tmem + col_o(wg);
+  const uint32_t n = a.n_kv;
+  uint32_t p_base0 = 0, p_base1 = 0;  // p_full completions before this item, per buffer
+  uint32_t q_used = 0;
+  RingPos s_pos;   // next K/V tile to wait for (S products, or release when idle)
+  RingPos pv_pos;  // next K/V tile whose V feeds a PV product
+  const bool acc0 = a.st.load != 0;
+  bool ok = true;
 
   // S[wg][buf] = Q_wg · K_stᵀ: K = 64 as four K=16 steps inside the swizzle atom.
-  auto issue_s = [&](uint32_t st, int buf) {
+  auto issue_s = [&](uint64_t q_desc, uint32_t st, int buf) {
     const uint64_t kd = k_desc + st * kKvTileStep;
     const uint32_t d = tmem + col_s(wg, buf);
 #pragma unroll
@@ -509,37 +547,72 @@ __device__ void mma_role(const Args& a, int wg, uint8_t* sQ, uint8_t* sK, uint8_
     for (int k = 0; k < kBN / 16; ++k)
       umma_ts_elect(o_tmem, p + 8 * k, vd + 128 * k, idesc_pv, (acc || k > 0) ? 1u : 0u);
   };
+  auto kv_wait = [&](const RingPos& r) {
+    return warp_wait(&ctl->kv_full[r.stage], r.phase, abort_flag, a.status, kSiteKvFull, a.timeout_ns);
+  };
 
-  bool ok = warp_wait(&ctl->q_full[wg], 0, abort_flag, a.status, kSiteQFull, a.timeout_ns);
-  if (ok) tc_fence_after();
-  // S(0) and S(1) up front.
-  for (uint32_t t = 0; ok && t < 2 && t < a.n_kv; ++t) {
-    if (!warp_wait(&ctl->kv_full[t % kStages], (t / kStages) & 1, abort_flag, a.status, kSiteKvFull,
-                   a.timeout_ns)) {
-      ok = false;
-      break;
+  for (uint32_t k = 0; ok; ++k) {
+    uint32_t item;
+    if (!next_item(a, ctl, k, &item)) break;
+    if (item >= a.n_items) break;
+    const Item it = decode_item(a, item);
+    if (it.row0 + wg * kBM >= a.t_q) {
+      // No rows for this warpgroup: release each stage once it has landed
+      // (waiting keeps this warp's view of the ring phases exact).
+      for (uint32_t j = 0; j < n; ++j, s_pos.next()) {
+        if (!kv_wait(s_pos)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_elect(&ctl->kv_empty[s_pos.stage]);
+      }
+      pv_pos = s_pos;
+      continue;
     }
-    issue_s(t % kStages, static_cast<int>(t));
-    umma_commit_elect(&ctl->s_full[wg][t]);
-  }
-  const bool acc0 = a.st.load != 0;
-  for (uint32_t j = 0; ok && j < a.n_kv; ++j) {
-    const int b = static_cast<int>(j & 1);
-    const uint32_t st = j % kStages;  // V_j: this stage was waited on before S(j) was issued
-    if (!warp_wait(&ctl->p_full[wg][b], (j >> 1) & 1, abort_flag, a.status, kSitePFull, a.timeout_ns)) break;
+    const uint32_t qb = q_used % kQBufs;
+    if (!warp_wait(&ctl->q_full[wg][qb], (q_used / kQBufs) & 1, abort_flag, a.status, kSiteQFull, a.timeout_ns))
+      break;
     tc_fence_after();
-    issue_pv(st, b, j > 0 || acc0);
-    if (j + 2 < a.n_kv) {
-      const uint32_t st2 = (j + 2) % kStages;
-      if (!warp_wait(&ctl->kv_full[st2], ((j + 2) / kStages) & 1, abort_flag, a.status, kSiteKvFull,
-                     a.timeout_ns)) {
+    const uint64_t q_desc = q_desc0 + qb * kQTileStep;
+    // S(0) and S(1) up front.  The commit after the item's last S also frees its Q buffer.
+    for (uint32_t t = 0; t < 2 && t < n; ++t) {
+      if (!kv_wait(s_pos)) {
         ok = false;
         break;
       }
-      issue_s(st2, b);  // after PV(j) in this warp's order, so it never overwrites P(j) early
+      issue_s(q_desc, s_pos.stage, static_cast<int>(t));
+      s_pos.next();
+      umma_commit_elect(&ctl->s_full[wg][t]);
+      if (t == n - 1) umma_commit_elect(&ctl->q_empty[wg][qb]);
     }
-    umma_commit_elect(&ctl->s_full[wg][b]);
-    if (j + kStages < a.n_kv) umma_commit_elect(&ctl->kv_empty[st]);  // the producer reuses this stage
+    for (uint32_t j = 0; ok && j < n; ++j) {
+      const int b = static_cast<int>(j & 1);
+      const uint32_t st = pv_pos.stage;  // V_j: this stage was waited on before S(j) was issued
+      pv_pos.next();
+      if (!warp_wait(&ctl->p_full[wg][b], ((b ? p_base1 : p_base0) + (j >> 1)) & 1, abort_flag, a.status,
+                     kSitePFull, a.timeout_ns)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      issue_pv(st, b, j > 0 || acc0);
+      if (j + 2 < n) {
+        if (!kv_wait(s_pos)) {
+          ok = false;
+          break;
+        }
+        issue_s(q_desc, s_pos.stage, b);  // after PV(j) in this warp's order: P(j) is read first
+        s_pos.next();
+        umma_commit_elect(&ctl->s_full[wg][b]);
+        if (j + 2 == n - 1) umma_commit_elect(&ctl->q_empty[wg][qb]);
+      } else {
+        umma_commit_elect(&ctl->pv_done[wg]);
+      }
+      umma_commit_elect(&ctl->kv_empty[st]);  // the producer may refill this stage
+    }
+    p_base0 += (n + 1) >> 1;
+    p_base1 += n >> 1;
+    ++q_used;
   }
   // Drain: every MMA this warp issued has completed before TMEM is freed.
   umma_commit_elect(&ctl->drain[wg]);
@@ -549,11 +622,12 @@ __device__ void mma_role(const Args& a, int wg, uint8_t* sQ, uint8_t* sK, uint8_
 
 template <typename E>
 __global__ void __launch_bounds__(kThreads, 1)
-    attn_fwd_sm100(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v, const Args a) {
+    attn_fwd_sm100(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                   const __grid_constant__ CUtensorMap tm_v, const Args a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
-  uint8_t* sK = sQ + 2 * kQTileBytes;
+  uint8_t* sK = sQ + 2 * kQBufs * kQTileBytes;
   uint8_t* sV = sK + kStages * kKvTileBytes;
   Ctrl* ctl = reinterpret_cast<Ctrl*>(sV + kStages * kKvTileBytes);
 
@@ -563,24 +637,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&ctl->kv_full[s], 1);
-      mbar_init(&ctl->kv_empty[s], 2);  // one commit per MMA warp
+      mbar_init(&ctl->kv_empty[s], 2);  // one arrival per MMA warp
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&ctl->q_full[i], kBM / 32);
+      for (int b = 0; b < kQBufs; ++b) {
+        mbar_init(&ctl->q_full[i][b], 1);
+        mbar_init(&ctl->q_empty[i][b], 1);
+      }
       for (int b = 0; b < 2; ++b) {
         mbar_init(&ctl->s_full[i][b], 1);
         mbar_init(&ctl->p_full[i][b], kBM / 32);
       }
+      mbar_init(&ctl->pv_done[i], 1);
       mbar_init(&ctl->drain[i], 1);
+    }
+    for (int i = 0; i < kItemSlots; ++i) {
+      mbar_init(&ctl->item_full[i], 1);
+      mbar_init(&ctl->item_empty[i], kItemReaders);
     }
     ctl->abort_flag = 0;
     fence_mbar_init();
   }
-  if (threadIdx.x < kD) {
-    ctl->ln_w[threadIdx.x] = a.qp.ln ? a.qp.ln_w[threadIdx.x] : 1.f;
-    ctl->ln_b[threadIdx.x] = a.qp.ln ? a.qp.ln_b[threadIdx.x] : 0.f;
-  }
   if (warp == kProducerWarp && lane == 0) {
+    tma_prefetch_desc(&tm_q);
     tma_prefetch_desc(&tm_k);
     tma_prefetch_desc(&tm_v);
   }
@@ -594,14 +673,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = ctl->tmem_base;
 
   // Launch budget 384 x 168 registers; softmax warpgroups take 224 each and
-  // the control warpgroup keeps 56: 2*224 + 56 == 3*168.
+  // the control warpgroup keeps 56: 2*224 + 56 == 3*168.  (The same code
+  // without the split, at 384 or 352 threads, measured 4-5 % slower.)
   if (warp < 8) {
     regs_inc<kSoftmaxRegs>();
-    softmax_role<E>(a, sQ, ctl, tmem, warp, lane);
+    softmax_role<E>(a, ctl, tmem, warp, lane);
   } else {
     regs_dec<kControlRegs>();
     if (warp == kProducerWarp) {
-      if (lane == 0) producer_role(a, &tm_k, &tm_v, sK, sV, ctl);
+      if (lane == 0) producer_role(a, &tm_q, &tm_k, &tm_v, sQ, sK, sV, ctl);
     } else if (warp == kMmaWarp0 || warp == kMmaWarp0 + 1) {
       mma_role<E>(a, warp - kMmaWarp0, sQ, sK, sV, ctl, tmem);
     }
@@ -612,6 +692,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == kTmemWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
+  }
+  // The last CTA to finish returns the counter to zero for the next launch
+  // on this stream (every fetch of every CTA happened before its arrival).
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(&a.sched[1], 1u) == gridDim.x - 1) {
+      atomicExch(&a.sched[0], 0u);
+      atomicExch(&a.sched[1], 0u);
+    }
   }
 }
 
@@ -631,9 +720,10 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// (SH, T, 64) 16-bit tensor as a 3-D map with kBN x 64 boxes, 128B swizzle.
-// Rows past T inside a sequence read as zeros (out-of-bounds fill).
-bool make_kv_map(CUtensorMap* map, const void* base, bool bf16, uint32_t t, uint32_t sh, std::string* err) {
+// (SH, T, 64) 16-bit tensor as a 3-D map with box_rows x 64 boxes, 128B
+// swizzle.  Rows past T inside a sequence read as zeros (out-of-bounds fill).
+bool make_map(CUtensorMap* map, const void* base, bool bf16, uint32_t t, uint32_t sh, uint32_t box_rows,
+              std::string* err) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) {
     if (err) *err = "cuTensorMapEncodeTiled unavailable";
@@ -641,7 +731,7 @@ bool make_kv_map(CUtensorMap* map, const void* base, bool bf16, uint32_t t, uint
   }
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(t), static_cast<cuuint64_t>(sh)};
   cuuint64_t strides[2] = {static_cast<cuuint64_t>(kD) * 2, static_cast<cuuint64_t>(t) * kD * 2};
-  cuuint32_t box[3] = {static_cast<cuuint32_t>(kD), static_cast<cuuint32_t>(kBN), 1};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(kD), box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -653,9 +743,23 @@ bool make_kv_map(CUtensorMap* map, const void* base, bool bf16, uint32_t t, uint
   return true;
 }
 
+int sm_count_of_current_device() {
+  static std::mutex mu;
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!cache[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
 template <typename E>
-cudaError_t launch_typed(cudaStream_t stream, const CUtensorMap& mk, const CUtensorMap& mv, const Args& a,
-                         uint32_t sh) {
+cudaError_t launch_typed(cudaStream_t stream, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                         const Args& a, uint32_t ctas) {
   static bool configured = false;
   if (!configured) {
     cudaError_t e =
@@ -663,36 +767,44 @@ cudaError_t launch_typed(cudaStream_t stream, const CUtensorMap& mk, const CUten
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  dim3 grid((a.t_q + 2 * kBM - 1) / (2 * kBM), sh, 1);
-  attn_fwd_sm100<E><<<grid, kThreads, kSmemBytes, stream>>>(mk, mv, a);
+  attn_fwd_sm100<E><<<ctas, kThreads, kSmemBytes, stream>>>(mq, mk, mv, a);
   return cudaGetLastError();
 }
 
 }  // namespace
 
-cudaError_t launch_attention_sm100(cudaStream_t stream, int elem, const void* q, int q_code, const void* k,
-                                   const void* v, void* out, int out_code, uint32_t sh, uint32_t t_q,
-                                   uint32_t t_kv, float scale, const QkPrologue& qp, const AttnState& st,
-                                   int* status, uint64_t timeout_ns, std::string* err) {
+cudaError_t launch_attention_sm100(cudaStream_t stream, int elem, const void* q, const void* k, const void* v,
+                                   void* out, int out_code, uint32_t sh, uint32_t t_q, uint32_t t_kv, float scale,
+                                   const AttnState& st, uint32_t max_ctas, int* status, uint32_t* sched,
+                                   uint64_t timeout_ns, std::string* err) {
   if (t_q == 0 || sh == 0) return cudaSuccess;
   const bool bf16 = elem == kBF16;
-  CUtensorMap mk, mv;
-  if (!make_kv_map(&mk, k, bf16, t_kv, sh, err) || !make_kv_map(&mv, v, bf16, t_kv, sh, err))
+  CUtensorMap mq, mk, mv;
+  if (!make_map(&mq, q, bf16, t_q, sh, kBM, err) || !make_map(&mk, k, bf16, t_kv, sh, kBN, err) ||
+      !make_map(&mv, v, bf16, t_kv, sh, kBN, err))
     return cudaErrorInvalidValue;
   Args a{};
-  a.q = q;
   a.out = out;
   a.t_q = t_q;
   a.t_kv = t_kv;
   a.n_kv = (t_kv + kBN - 1) / kBN;
-  a.q_f32 = q_code == kF32;
+  a.pairs = (t_q + kItemRows - 1) / kItemRows;
+  const uint64_t items = static_cast<uint64_t>(sh) * a.pairs;
+  if (items > 0x7fffffffull) {
+    if (err) *err = "too many work items";
+    return cudaErrorInvalidValue;
+  }
+  a.n_items = static_cast<uint32_t>(items);
   a.out_f32 = out_code == kF32;
   a.scale_log2 = scale * 1.4426950408889634f;
-  a.qp = qp;
   a.st = st;
   a.status = status;
+  a.sched = sched;
   a.timeout_ns = timeout_ns;
-  return bf16 ? launch_typed<__nv_bfloat16>(stream, mk, mv, a, sh) : launch_typed<__half>(stream, mk, mv, a, sh);
+  uint32_t ctas = max_ctas ? max_ctas : static_cast<uint32_t>(sm_count_of_current_device());
+  if (ctas > a.n_items) ctas = a.n_items;
+  return bf16 ? launch_typed<__nv_bfloat16>(stream, mq, mk, mv, a, ctas)
+              : launch_typed<__half>(stream, mq, mk, mv, a, ctas);
 }
 
 }  // namespace hs

@@ -24,6 +24,7 @@ struct hs_ctx {
   cudaStream_t user_stream = nullptr;  // borrowed (hs_ctx_set_stream); may be the legacy stream 0
   bool has_user_stream = false;
   int* d_status = nullptr;             // device status word: first bounded-wait site that timed out
+  uint32_t* d_sched = nullptr;         // attention work counter pair (d_status + 2), zero between launches
   void* scratch = nullptr;             // normalised/rotated K (and 16-bit V for f32 callers)
   size_t scratch_bytes = 0;
   uint32_t wait_timeout_ms = 2000;

@@ -39,14 +39,16 @@ struct AttnState {
   int store = 0;       // write the state instead of the normalised output
 };
 
-// Fused flash attention on tcgen05 (D = 64).  Keys/values are 16-bit
-// (`elem` = kF16 or kBF16); q may be 16-bit of the same type or f32;
-// out is written in `out_code` (kF32 or `elem`).  The Q tile receives the
-// QK-norm/RoPE prologue in-kernel; K must already be normalised/rotated.
-cudaError_t launch_attention_sm100(cudaStream_t stream, int elem, const void* q, int q_code, const void* k,
-                                   const void* v, void* out, int out_code, uint32_t sh, uint32_t t_q,
-                                   uint32_t t_kv, float scale, const QkPrologue& qp, const AttnState& st,
-                                   int* status, uint64_t timeout_ns, std::string* err);
+// Flash attention on tcgen05 (D = 64), persistent: at most `max_ctas` CTAs
+// (0 = one per SM) take the (sequence, 256-row) work items from the counter
+// pair `sched` (2 x u32, zero before the launch; the kernel leaves it zero,
+// so launches sharing it must be ordered on one stream).  q, k and v are
+// 16-bit rows of `elem` (kF16 or kBF16) with any QK-norm/RoPE already
+// applied (qk_prep); out is written in `out_code` (kF32 or `elem`).
+cudaError_t launch_attention_sm100(cudaStream_t stream, int elem, const void* q, const void* k, const void* v,
+                                   void* out, int out_code, uint32_t sh, uint32_t t_q, uint32_t t_kv, float scale,
+                                   const AttnState& st, uint32_t max_ctas, int* status, uint32_t* sched,
+                                   uint64_t timeout_ns, std::string* err);
 
 // Row prep for K (and for casts): out = RoPE(LN(x)) in `out_code` storage.
 cudaError_t launch_qk_prep(cudaStream_t stream, const void* x, int in_code, void* out, int out_code,

@@ -6,8 +6,8 @@
 // fixed, pre-reserved pool (an embedding engine, a Rust host that budgets
 // every buffer up front), and session loops that must not stall or fail on
 // an allocation once they are running.  hs_attention_fused grows a scratch
-// buffer with cudaMallocAsync for the normalised/rotated K; this variant
-// uses a fixed array compiled into the library instead and calls no
+// buffer with cudaMallocAsync for the normalised/rotated Q and K; this
+// variant uses a fixed array compiled into the library instead and calls no
 // cudaMalloc, cudaFree or other allocating routine.
 //
 // The array is a file-scope __device__ object, so every GPU that loads the
@@ -27,24 +27,28 @@
 
 namespace {
 
-constexpr size_t kNoAllocScratchBytes = static_cast<size_t>(HS_NOALLOC_MAX_ROWS) * 64 * 2;
+constexpr size_t kNoAllocRegionBytes = static_cast<size_t>(HS_NOALLOC_MAX_ROWS) * 64 * 2;
+constexpr size_t kNoAllocScratchBytes = 2 * kNoAllocRegionBytes;  // Q rows, then K rows
 constexpr int kMaxDevices = 64;
 constexpr uint64_t kNoAllocTimeoutNs = 2000ull * 1000000ull;
 
-// Normalised/rotated K rows (16-bit, 128 bytes per row of D = 64).
+// Normalised/rotated Q rows, then K rows (16-bit, 128 bytes per row of D = 64).
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 // Bounded-wait status word used when the caller passes no status pointer.
 static __device__ __align__(256) int g_noalloc_status[4];
+// Work counter pair of the persistent attention kernel (zero between calls).
+static __device__ __align__(256) uint32_t g_noalloc_sched[2];
 
 struct DevicePtrs {
   void* scratch = nullptr;
   int* status = nullptr;
+  uint32_t* sched = nullptr;
 };
 
 std::mutex g_mu;
 DevicePtrs g_ptrs[kMaxDevices];
 
-// Device addresses of the two arrays on the current device, looked up once
+// Device addresses of the three arrays on the current device, looked up once
 // per device.  In host code the arrays' names only stand for the symbols;
 // cudaGetSymbolAddress turns them into device addresses.
 hs_status device_ptrs(int dev, DevicePtrs* out) {
@@ -61,8 +65,14 @@ hs_status device_ptrs(int dev, DevicePtrs* out) {
     if (e != cudaSuccess)
       return hs::abi_fail(HS_ERR_CUDA, std::string("hs_attention_fused_noalloc: status address: ") +
                                            cudaGetErrorString(e));
+    void* sc = nullptr;
+    e = cudaGetSymbolAddress(&sc, g_noalloc_sched);
+    if (e != cudaSuccess)
+      return hs::abi_fail(HS_ERR_CUDA, std::string("hs_attention_fused_noalloc: counter address: ") +
+                                           cudaGetErrorString(e));
     p.scratch = s;
     p.status = static_cast<int*>(st);
+    p.sched = static_cast<uint32_t*>(sc);
   }
   *out = p;
   return HS_OK;
@@ -136,16 +146,21 @@ extern "C" hs_status hs_attention_fused_noalloc(void* stream, int* status, const
   kp.ln_w = k_norm_w;
   kp.ln_b = k_norm_b;
   const int code = static_cast<int>(dtype);
+  const void* q_use = q;
   const void* k_use = k;
   if (ln || rope) {
-    e = hs::launch_qk_prep(st, k, code, p.scratch, code, rows, T, kp);
+    uint8_t* q_rows = static_cast<uint8_t*>(p.scratch);
+    uint8_t* k_rows = q_rows + kNoAllocRegionBytes;
+    e = hs::launch_qk_prep(st, q, code, q_rows, code, rows, T, qp);
+    if (e == cudaSuccess) e = hs::launch_qk_prep(st, k, code, k_rows, code, rows, T, kp);
     if (e != cudaSuccess) return hs::abi_cuda_fail(e, name);
-    k_use = p.scratch;
+    q_use = q_rows;
+    k_use = k_rows;
   }
   std::string err;
   hs::AttnState state{};
-  e = hs::launch_attention_sm100(st, code, q, code, k_use, v, out, code, S * H, T, T, scale, qp, state, status_word,
-                                 kNoAllocTimeoutNs, &err);
+  e = hs::launch_attention_sm100(st, code, q_use, k_use, v, out, code, S * H, T, T, scale, state, 0, status_word,
+                                 p.sched, kNoAllocTimeoutNs, &err);
   if (e != cudaSuccess)
     return hs::abi_fail(HS_ERR_CUDA, std::string(name) + ": " + (err.empty() ? cudaGetErrorString(e) : err));
   return HS_OK;

@@ -66,6 +66,7 @@ __device__ __forceinline__ void store8(T* p, const float (&v)[8]) {
 
 constexpr int kPrepTokens = 32;     // tokens per block (8 threads per 64-wide row)
 constexpr int kPrepSeqPerBlock = 16;  // sequences (s, h) a block sweeps with one staged table slice
+constexpr int kPrepBatch = 4;         // of those, rows loaded back to back by one thread
 
 // K' = RoPE(LN(x)) over (SH, T, 64).  A block owns kPrepTokens consecutive
 // tokens of up to kPrepSeqPerBlock sequences: the sin/cos rows of its tokens
@@ -112,49 +113,55 @@ __global__ void __launch_bounds__(256) qk_prep_kernel(const In* __restrict__ x, 
     bb[i] = p.ln ? __ldg(p.ln_b + 8 * g + i) : 0.f;
   }
   const uint32_t seq_end = min(sh, (blockIdx.y + 1) * kPrepSeqPerBlock);
-  for (uint32_t q = blockIdx.y * kPrepSeqPerBlock; q < seq_end; ++q) {
-    const uint64_t row = static_cast<uint64_t>(q) * t + tok;
-    float v[8];
-    if (tok_ok) {
-      load8(x + row * 64 + 8 * g, v);
-    } else {
+  // kPrepBatch rows in flight per thread: their loads are issued together.
+  for (uint32_t q0 = blockIdx.y * kPrepSeqPerBlock; q0 < seq_end; q0 += kPrepBatch) {
+    float v[kPrepBatch][8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) v[i] = 0.f;
-    }
-    if (p.ln) {
-      float sm = 0.f;
+    for (int u = 0; u < kPrepBatch; ++u) {
+      if (tok_ok && q0 + u < seq_end) {
+        load8(x + (static_cast<uint64_t>(q0 + u) * t + tok) * 64 + 8 * g, v[u]);
+      } else {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) sm += v[i];
-      sm += __shfl_xor_sync(0xffffffffu, sm, 1);
-      sm += __shfl_xor_sync(0xffffffffu, sm, 2);
-      sm += __shfl_xor_sync(0xffffffffu, sm, 4);
-      const float mu = sm * (1.0f / 64);
-      float sq = 0.f;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float d = v[i] - mu;
-        sq = fmaf(d, d, sq);
-      }
-      sq += __shfl_xor_sync(0xffffffffu, sq, 1);
-      sq += __shfl_xor_sync(0xffffffffu, sq, 2);
-      sq += __shfl_xor_sync(0xffffffffu, sq, 4);
-      const float inv = rsqrtf(sq * (1.0f / 64) + p.eps);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) v[i] = (v[i] - mu) * inv * w[i] + bb[i];
-    }
-    if (p.rope) {
-      float pv[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) pv[i] = __shfl_xor_sync(0xffffffffu, v[i], 4);
-      // Pass-through rows hold sin 0 / cos 1, so every row takes the same path.
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float sn = sin_s[lt][8 * g + i], cs = cos_s[lt][8 * g + i];
-        // lower half: x*cos - x[i+32]*sin ; upper half: x*cos + x[i-32]*sin
-        v[i] = g < 4 ? v[i] * cs - pv[i] * sn : v[i] * cs + pv[i] * sn;
+        for (int i = 0; i < 8; ++i) v[u][i] = 0.f;
       }
     }
-    if (tok_ok) store8(out + row * 64 + 8 * g, v);
+#pragma unroll
+    for (int u = 0; u < kPrepBatch; ++u) {
+      if (p.ln) {
+        float sm = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) sm += v[u][i];
+        sm += __shfl_xor_sync(0xffffffffu, sm, 1);
+        sm += __shfl_xor_sync(0xffffffffu, sm, 2);
+        sm += __shfl_xor_sync(0xffffffffu, sm, 4);
+        const float mu = sm * (1.0f / 64);
+        float sq = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float d = v[u][i] - mu;
+          sq = fmaf(d, d, sq);
+        }
+        sq += __shfl_xor_sync(0xffffffffu, sq, 1);
+        sq += __shfl_xor_sync(0xffffffffu, sq, 2);
+        sq += __shfl_xor_sync(0xffffffffu, sq, 4);
+        const float inv = rsqrtf(sq * (1.0f / 64) + p.eps);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[u][i] = (v[u][i] - mu) * inv * w[i] + bb[i];
+      }
+      if (p.rope) {
+        float pv[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) pv[i] = __shfl_xor_sync(0xffffffffu, v[u][i], 4);
+        // Pass-through rows hold sin 0 / cos 1, so every row takes the same path.
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float sn = sin_s[lt][8 * g + i], cs = cos_s[lt][8 * g + i];
+          // lower half: x*cos - x[i+32]*sin ; upper half: x*cos + x[i-32]*sin
+          v[u][i] = g < 4 ? v[u][i] * cs - pv[i] * sn : v[u][i] * cs + pv[i] * sn;
+        }
+      }
+      if (tok_ok && q0 + u < seq_end) store8(out + (static_cast<uint64_t>(q0 + u) * t + tok) * 64 + 8 * g, v[u]);
+    }
   }
 }
 

@@ -108,7 +108,9 @@ struct hs_ring {
   cudaEvent_t ev_done = nullptr;
   void* buf[2] = {nullptr, nullptr};
   size_t buf_bytes = 0;
-  float* state = nullptr;  // o (rows x 64) | m (rows) | l (rows)
+  // Per query row of this rank's shard: the normalised/rotated q (64 x 16-bit),
+  // then the carried softmax state o (64 f32) | m (f32) | l (f32).
+  uint8_t* state = nullptr;
   size_t state_rows = 0;
   bool aborted = false;
 };
@@ -259,7 +261,7 @@ hs_status hs_ring_attention_fused(hs_ring* ring, const void* q, const void* k, c
     cudaStreamSynchronize(st);
     if (ring->state) cudaFree(ring->state);
     ring->state = nullptr;
-    e = cudaMalloc(&ring->state, rows * 66 * sizeof(float));
+    e = cudaMalloc(&ring->state, rows * (row_bytes + 66 * sizeof(float)));
     if (e != cudaSuccess) return hs::abi_cuda_fail(e, "ring state");
     ring->state_rows = rows;
   }
@@ -296,10 +298,20 @@ hs_status hs_ring_attention_fused(hs_ring* ring, const void* q, const void* k, c
   if (e != cudaSuccess) return hs::abi_cuda_fail(e, "ring V copy");
   cudaEventRecord(ring->ev_block0, st);
 
+  const void* q_use = q;
+  if (ln || rope) {
+    {
+      hs::ProfScope prof(ctx, st, "qk_prep");
+      e = hs::launch_qk_prep(st, q, code, ring->state, code, rows, tr, qp);
+    }
+    if (e != cudaSuccess) return hs::abi_cuda_fail(e, "ring Q' prep");
+    q_use = ring->state;
+  }
   hs::AttnState state{};
-  state.o = ring->state;
-  state.m = ring->state + rows * 64;
-  state.l = ring->state + rows * 65;
+  float* state_f = reinterpret_cast<float*>(ring->state + rows * row_bytes);
+  state.o = state_f;
+  state.m = state_f + rows * 64;
+  state.l = state_f + rows * 65;
   for (int s = 0; s < R; ++s) {
     int src, send_to, recv_from, load, store;
     hs_ring_plan(r, R, s, &src, &send_to, &recv_from, &load, &store);
@@ -327,8 +339,8 @@ hs_status hs_ring_attention_fused(hs_ring* ring, const void* q, const void* k, c
     std::string err;
     {
       hs::ProfScope prof(ctx, st, "attention");
-      e = hs::launch_attention_sm100(st, code, q, code, cur, cur + static_cast<size_t>(H) * src_len * row_bytes,
-                                     out, code, H, tr, src_len, scale, qp, state, ctx->d_status,
+      e = hs::launch_attention_sm100(st, code, q_use, cur, cur + static_cast<size_t>(H) * src_len * row_bytes, out,
+                                     code, H, tr, src_len, scale, state, 0, ctx->d_status, ctx->d_sched,
                                      hs::ctx_timeout_ns(ctx), &err);
     }
     if (e != cudaSuccess)

@@ -135,9 +135,9 @@ HS_API hs_status hs_attention_fused(hs_ctx* ctx, const void* q, const void* k, c
  * loops that must not stall or fail on an allocation once running.  Same
  * arguments and results as hs_attention_fused (f16/bf16 storage only), but
  * no hs_ctx: work goes on `stream` (a cudaStream_t, NULL = legacy default
- * stream) of the current device, and the normalised K lives in a fixed
- * array inside the library — HS_NOALLOC_MAX_ROWS rows of 128 bytes (32 MiB),
- * held by every GPU that loads the library until the process exits.
+ * stream) of the current device, and the normalised Q and K live in a fixed
+ * array inside the library — 2 x HS_NOALLOC_MAX_ROWS rows of 128 bytes
+ * (64 MiB), held by every GPU that loads the library until the process exits.
  * S*H*T above HS_NOALLOC_MAX_ROWS returns HS_ERR_INVALID.
  * The first call on a device looks up that array's device address (no
  * allocation by this library); make that first call before any stream
