@@ -132,8 +132,14 @@ hs_status attention_impl(hs_ctx* ctx, const void* q, const void* k, const void* 
   }
   const void* use[3] = {q, k, v};
   const bool direct[3] = {q_direct, k_direct, v_direct};
+  // When both q and k pass through qk_prep it also records their largest
+  // row norms, which let the attention kernel bound every score.
+  unsigned int* norm2 = (!q_direct && !k_direct) ? ctx->d_norm2 : nullptr;
+  QkPrologue qpn = qp, kpn = kp;
+  qpn.norm2_max = norm2;
+  kpn.norm2_max = norm2 ? norm2 + 1 : nullptr;
   const QkPrologue none{};
-  const QkPrologue* pro[3] = {&qp, &kp, &none};
+  const QkPrologue* pro[3] = {&qpn, &kpn, &none};
   static const char* const what[3] = {"qk_prep(q)", "qk_prep(k)", "cast(v)"};
   uint8_t* cursor = static_cast<uint8_t*>(scratch);
   cudaError_t e;
@@ -152,7 +158,7 @@ hs_status attention_impl(hs_ctx* ctx, const void* q, const void* k, const void* 
   {
     ProfScope prof(ctx, st, "attention");
     e = launch_attention_sm100(st, elem, use[0], use[1], use[2], out, code == kF32 ? kF32 : elem, S * H, T, T,
-                               scale, state, 0, ctx->d_status, ctx->d_sched, ctx_timeout_ns(ctx), &err);
+                               scale, state, 0, ctx->d_status, ctx->d_sched, norm2, ctx_timeout_ns(ctx), &err);
   }
   if (e != cudaSuccess) return fail(HS_ERR_CUDA, std::string(name) + ": " + (err.empty() ? cudaGetErrorString(e) : err));
   return HS_OK;
@@ -190,9 +196,11 @@ hs_status hs_ctx_create(int device, hs_ctx** out) {
     delete ctx;
     return cuda_fail(e, "hs_ctx_create: stream");
   }
-  e = cudaMalloc(&ctx->d_status, sizeof(int) * 4);
-  if (e == cudaSuccess) e = cudaMemset(ctx->d_status, 0, sizeof(int) * 4);
+  // [0] status word, [2..3] attention work counter, [4..5] q'/k' norm bounds.
+  e = cudaMalloc(&ctx->d_status, sizeof(int) * 8);
+  if (e == cudaSuccess) e = cudaMemset(ctx->d_status, 0, sizeof(int) * 8);
   ctx->d_sched = reinterpret_cast<uint32_t*>(ctx->d_status + 2);
+  ctx->d_norm2 = reinterpret_cast<unsigned int*>(ctx->d_status + 4);
   if (e != cudaSuccess) {
     cudaStreamDestroy(ctx->stream);
     delete ctx;

@@ -128,6 +128,9 @@ static_assert(kSmemBytes <= 232448, "shared memory per CTA");
 
 struct Args {
   void* out;
+  // Max squared norms of the q' and k' rows (f32 bit patterns, set by
+  // qk_prep), or null.  Zeroed by the last CTA, ready for the next call.
+  unsigned int* qk_norm2;
   uint32_t t_q;      // query rows per sequence
   uint32_t t_kv;     // keys per sequence
   uint32_t n_kv;     // ceil(t_kv / kBN)
@@ -249,8 +252,12 @@ __device__ __forceinline__ void exp2_poly2(float x0, float x1, float& y0, float&
   y1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
 }
 
-template <typename E>
-__device__ void softmax_role(const Args& a, Ctrl* ctl, uint32_t tmem, int warp, int lane) {
+// kFixed: every score is known to satisfy |s*c| <= m_fixed (Cauchy-Schwarz
+// on the stored q' and k' rows), so P = 2^(s*c - m_fixed) <= 1 for a fixed
+// offset: no row max, no rescale.  Used when m_fixed is small enough that
+// every P of a valid key stays far inside the 16-bit type's normal range.
+template <typename E, bool kFixed>
+__device__ void softmax_role(const Args& a, Ctrl* ctl, uint32_t tmem, int warp, int lane, float m_fixed) {
   const int wg = warp >> 2;
   const int wq = warp & 3;
   const uint32_t row = static_cast<uint32_t>(wq * 32 + lane);
@@ -281,7 +288,7 @@ __device__ void softmax_role(const Args& a, Ctrl* ctl, uint32_t tmem, int warp, 
     const bool valid = token < a.t_q;
     const uint64_t row_index = static_cast<uint64_t>(it.seq) * a.t_q + token;
 
-    float m_run = -INFINITY, l = 0.f;
+    float m_run = kFixed ? m_fixed : -INFINITY, l = 0.f;
     bool have_o = false;
     if (a.st.load && valid) {
       m_run = a.st.m[row_index];
@@ -324,21 +331,22 @@ __device__ void softmax_role(const Args& a, Ctrl* ctl, uint32_t tmem, int warp, 
         for (int i = 0; i < kBN; ++i)
           if (static_cast<uint32_t>(i) >= tail) s[i] = __float_as_uint(-INFINITY);
       }
-      // Row max: 3-input max in four independent chains.
-      float m4[4] = {u2f(s[0]), u2f(s[1]), u2f(s[2]), u2f(s[3])};
-#pragma unroll
-      for (int i = 4; i < kBN; i += 2) m4[(i >> 1) & 3] = max3(m4[(i >> 1) & 3], u2f(s[i]), u2f(s[i + 1]));
-      const float m_tile = max3(fmaxf(m4[0], m4[1]), m4[2], m4[3]) * c;
-
       float factor = 1.f;
       bool need = false;
-      if (!have_o) {
-        m_run = m_tile;
-      } else if (m_tile > m_run + kRescaleThreshold) {
-        factor = ex2_approx(m_run - m_tile);
-        m_run = m_tile;
-        l *= factor;
-        need = true;
+      if constexpr (!kFixed) {
+        // Row max: 3-input max in four independent chains.
+        float m4[4] = {u2f(s[0]), u2f(s[1]), u2f(s[2]), u2f(s[3])};
+#pragma unroll
+        for (int i = 4; i < kBN; i += 2) m4[(i >> 1) & 3] = max3(m4[(i >> 1) & 3], u2f(s[i]), u2f(s[i + 1]));
+        const float m_tile = max3(fmaxf(m4[0], m4[1]), m4[2], m4[3]) * c;
+        if (!have_o) {
+          m_run = m_tile;
+        } else if (m_tile > m_run + kRescaleThreshold) {
+          factor = ex2_approx(m_run - m_tile);
+          m_run = m_tile;
+          l *= factor;
+          need = true;
+        }
       }
       // P = 2^(s*c - m) on packed f32x2 pairs; kEmuPer8 of every 8 pairs take
       // the FMA-pipe exp2, the rest MUFU.EX2.  P overwrites the first kPairs
@@ -368,7 +376,7 @@ __device__ void softmax_role(const Args& a, Ctrl* ctl, uint32_t tmem, int warp, 
       // together with S(j+1) when that tile exists, else (j = n-1) as the
       // item's first PV-only batch.  PV(j) is issued only after p_full, so it
       // accumulates onto the rescaled O.
-      if (__any_sync(0xffffffffu, need)) {
+      if (!kFixed && __any_sync(0xffffffffu, need)) {
         if (j > 0) {
           const bool ok = (j + 1 < n) ? warp_wait(&ctl->s_full[wg][(j + 1) & 1], s_parity(j + 1), abort_flag,
                                                   a.status, kSiteODone, a.timeout_ns)
@@ -442,6 +450,27 @@ __device__ void softmax_role(const Args& a, Ctrl* ctl, uint32_t tmem, int warp, 
       a.st.l[row_index] = l;
     }
   }
+}
+
+// Largest offset for the fixed-offset softmax: valid keys keep P >=
+// 2^(-2 * limit), inside the normal range with room to spare (bf16: 2^-96,
+// ~30 binades above what a masked key can round to; f16: 2^-14).
+template <typename E>
+__host__ __device__ constexpr float fixed_offset_limit() { return Elem<E>::kBf16 ? 48.f : 7.f; }
+
+template <typename E>
+__device__ void softmax_dispatch(const Args& a, Ctrl* ctl, uint32_t tmem, int warp, int lane) {
+  float bound = INFINITY;
+  if (a.qk_norm2 && !a.st.load && !a.st.store) {
+    const float qn = sqrtf(__uint_as_float(a.qk_norm2[0]));
+    const float kn = sqrtf(__uint_as_float(a.qk_norm2[1]));
+    // Margin for the f32 accumulation inside the tensor core.
+    bound = qn * kn * a.scale_log2 * 1.0009765625f + 1e-3f;
+  }
+  if (bound <= fixed_offset_limit<E>())
+    softmax_role<E, true>(a, ctl, tmem, warp, lane, bound);
+  else
+    softmax_role<E, false>(a, ctl, tmem, warp, lane, 0.f);
 }
 
 // One thread.  Per item: the Q tiles of the warpgroups with rows in it, then
@@ -677,7 +706,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // without the split, at 384 or 352 threads, measured 4-5 % slower.)
   if (warp < 8) {
     regs_inc<kSoftmaxRegs>();
-    softmax_role<E>(a, ctl, tmem, warp, lane);
+    softmax_dispatch<E>(a, ctl, tmem, warp, lane);
   } else {
     regs_dec<kControlRegs>();
     if (warp == kProducerWarp) {
@@ -700,6 +729,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (atomicAdd(&a.sched[1], 1u) == gridDim.x - 1) {
       atomicExch(&a.sched[0], 0u);
       atomicExch(&a.sched[1], 0u);
+      if (a.qk_norm2) {  // every CTA read the bounds at its start
+        atomicExch(&a.qk_norm2[0], 0u);
+        atomicExch(&a.qk_norm2[1], 0u);
+      }
     }
   }
 }
@@ -776,7 +809,7 @@ cudaError_t launch_typed(cudaStream_t stream, const CUtensorMap& mq, const CUten
 cudaError_t launch_attention_sm100(cudaStream_t stream, int elem, const void* q, const void* k, const void* v,
                                    void* out, int out_code, uint32_t sh, uint32_t t_q, uint32_t t_kv, float scale,
                                    const AttnState& st, uint32_t max_ctas, int* status, uint32_t* sched,
-                                   uint64_t timeout_ns, std::string* err) {
+                                   unsigned int* qk_norm2, uint64_t timeout_ns, std::string* err) {
   if (t_q == 0 || sh == 0) return cudaSuccess;
   const bool bf16 = elem == kBF16;
   CUtensorMap mq, mk, mv;
@@ -800,6 +833,7 @@ cudaError_t launch_attention_sm100(cudaStream_t stream, int elem, const void* q,
   a.st = st;
   a.status = status;
   a.sched = sched;
+  a.qk_norm2 = qk_norm2;
   a.timeout_ns = timeout_ns;
   uint32_t ctas = max_ctas ? max_ctas : static_cast<uint32_t>(sm_count_of_current_device());
   if (ctas > a.n_items) ctas = a.n_items;

@@ -25,6 +25,7 @@ struct hs_ctx {
   bool has_user_stream = false;
   int* d_status = nullptr;             // device status word: first bounded-wait site that timed out
   uint32_t* d_sched = nullptr;         // attention work counter pair (d_status + 2), zero between launches
+  unsigned int* d_norm2 = nullptr;     // q'/k' max squared row norms (d_status + 4), zero between launches
   void* scratch = nullptr;             // normalised/rotated K (and 16-bit V for f32 callers)
   size_t scratch_bytes = 0;
   uint32_t wait_timeout_ms = 2000;

@@ -26,6 +26,9 @@ struct QkPrologue {
   uint32_t tokens_per_frame = 0;  // table row of token t is (t mod tpf) - prefix
   int rope = 0;
   uint32_t pos_offset = 0;  // global index of this shard's token 0 (ring shards)
+  // When set, raised (atomicMax on the f32 bit pattern) to the largest
+  // squared norm of the rows written, as stored (after 16-bit rounding).
+  unsigned int* norm2_max = nullptr;
 };
 
 // Running softmax state for attention split over several launches (ring
@@ -45,10 +48,14 @@ struct AttnState {
 // so launches sharing it must be ordered on one stream).  q, k and v are
 // 16-bit rows of `elem` (kF16 or kBF16) with any QK-norm/RoPE already
 // applied (qk_prep); out is written in `out_code` (kF32 or `elem`).
+// `qk_norm2` (2 x u32 or null): the max squared row norms of q and k as
+// qk_prep recorded them; when they bound every score tightly enough the
+// softmax uses a fixed offset instead of a running max.  Zeroed by the
+// kernel.
 cudaError_t launch_attention_sm100(cudaStream_t stream, int elem, const void* q, const void* k, const void* v,
                                    void* out, int out_code, uint32_t sh, uint32_t t_q, uint32_t t_kv, float scale,
                                    const AttnState& st, uint32_t max_ctas, int* status, uint32_t* sched,
-                                   uint64_t timeout_ns, std::string* err);
+                                   unsigned int* qk_norm2, uint64_t timeout_ns, std::string* err);
 
 // Row prep for K (and for casts): out = RoPE(LN(x)) in `out_code` storage.
 cudaError_t launch_qk_prep(cudaStream_t stream, const void* x, int in_code, void* out, int out_code,

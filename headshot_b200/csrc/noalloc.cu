@@ -36,8 +36,9 @@ constexpr uint64_t kNoAllocTimeoutNs = 2000ull * 1000000ull;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 // Bounded-wait status word used when the caller passes no status pointer.
 static __device__ __align__(256) int g_noalloc_status[4];
-// Work counter pair of the persistent attention kernel (zero between calls).
-static __device__ __align__(256) uint32_t g_noalloc_sched[2];
+// Work counter pair of the persistent attention kernel, then the q'/k'
+// max squared row norms (all zero between calls).
+static __device__ __align__(256) uint32_t g_noalloc_sched[4];
 
 struct DevicePtrs {
   void* scratch = nullptr;
@@ -151,6 +152,8 @@ extern "C" hs_status hs_attention_fused_noalloc(void* stream, int* status, const
   if (ln || rope) {
     uint8_t* q_rows = static_cast<uint8_t*>(p.scratch);
     uint8_t* k_rows = q_rows + kNoAllocRegionBytes;
+    qp.norm2_max = p.sched + 2;
+    kp.norm2_max = p.sched + 3;
     e = hs::launch_qk_prep(st, q, code, q_rows, code, rows, T, qp);
     if (e == cudaSuccess) e = hs::launch_qk_prep(st, k, code, k_rows, code, rows, T, kp);
     if (e != cudaSuccess) return hs::abi_cuda_fail(e, name);
@@ -160,7 +163,7 @@ extern "C" hs_status hs_attention_fused_noalloc(void* stream, int* status, const
   std::string err;
   hs::AttnState state{};
   e = hs::launch_attention_sm100(st, code, q_use, k_use, v, out, code, S * H, T, T, scale, state, 0, status_word,
-                                 p.sched, kNoAllocTimeoutNs, &err);
+                                 p.sched, (ln || rope) ? p.sched + 2 : nullptr, kNoAllocTimeoutNs, &err);
   if (e != cudaSuccess)
     return hs::abi_fail(HS_ERR_CUDA, std::string(name) + ": " + (err.empty() ? cudaGetErrorString(e) : err));
   return HS_OK;

@@ -49,6 +49,24 @@ __device__ __forceinline__ void load8(const T* p, float (&v)[8]) {
   }
 }
 
+// Squared norm of 8 values as a T store would round them.
+template <typename T>
+__device__ __forceinline__ float stored_norm2(const float (&v)[8]) {
+  float n2 = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; i += 2) {
+    float2 r;
+    if constexpr (sizeof(T) == 4) {
+      r = make_float2(v[i], v[i + 1]);
+    } else {
+      r = Elem<T>::unpack2(Elem<T>::pack2(v[i], v[i + 1]));
+    }
+    n2 = fmaf(r.x, r.x, n2);
+    n2 = fmaf(r.y, r.y, n2);
+  }
+  return n2;
+}
+
 template <typename T>
 __device__ __forceinline__ void store8(T* p, const float (&v)[8]) {
   if constexpr (sizeof(T) == 4) {
@@ -113,6 +131,7 @@ __global__ void __launch_bounds__(256) qk_prep_kernel(const In* __restrict__ x, 
     bb[i] = p.ln ? __ldg(p.ln_b + 8 * g + i) : 0.f;
   }
   const uint32_t seq_end = min(sh, (blockIdx.y + 1) * kPrepSeqPerBlock);
+  float n2_max = 0.f;
   // kPrepBatch rows in flight per thread: their loads are issued together.
   for (uint32_t q0 = blockIdx.y * kPrepSeqPerBlock; q0 < seq_end; q0 += kPrepBatch) {
     float v[kPrepBatch][8];
@@ -160,8 +179,23 @@ __global__ void __launch_bounds__(256) qk_prep_kernel(const In* __restrict__ x, 
           v[u][i] = g < 4 ? v[u][i] * cs - pv[i] * sn : v[u][i] * cs + pv[i] * sn;
         }
       }
-      if (tok_ok && q0 + u < seq_end) store8(out + (static_cast<uint64_t>(q0 + u) * t + tok) * 64 + 8 * g, v[u]);
+      const bool row_ok = tok_ok && q0 + u < seq_end;
+      if (row_ok) store8(out + (static_cast<uint64_t>(q0 + u) * t + tok) * 64 + 8 * g, v[u]);
+      if (p.norm2_max) {  // uniform branch: the row's 8 lanes add their parts
+        float n2 = row_ok ? stored_norm2<Out>(v[u]) : 0.f;
+        n2 += __shfl_xor_sync(0xffffffffu, n2, 1);
+        n2 += __shfl_xor_sync(0xffffffffu, n2, 2);
+        n2 += __shfl_xor_sync(0xffffffffu, n2, 4);
+        n2_max = fmaxf(n2_max, n2);
+      }
     }
+  }
+  if (p.norm2_max) {
+    // Max across the warp's 4 rows, one atomic per warp (non-negative
+    // floats order like their bit patterns).
+    n2_max = fmaxf(n2_max, __shfl_xor_sync(0xffffffffu, n2_max, 8));
+    n2_max = fmaxf(n2_max, __shfl_xor_sync(0xffffffffu, n2_max, 16));
+    if ((threadIdx.x & 31) == 0) atomicMax(p.norm2_max, __float_as_uint(n2_max));
   }
 }
 

@@ -341,7 +341,7 @@ hs_status hs_ring_attention_fused(hs_ring* ring, const void* q, const void* k, c
       hs::ProfScope prof(ctx, st, "attention");
       e = hs::launch_attention_sm100(st, code, q_use, cur, cur + static_cast<size_t>(H) * src_len * row_bytes, out,
                                      code, H, tr, src_len, scale, state, 0, ctx->d_status, ctx->d_sched,
-                                     hs::ctx_timeout_ns(ctx), &err);
+                                     nullptr, hs::ctx_timeout_ns(ctx), &err);
     }
     if (e != cudaSuccess)
       return hs::abi_fail(HS_ERR_CUDA, std::string(name) + ": " + (err.empty() ? cudaGetErrorString(e) : err));

@@ -66,6 +66,30 @@ def test_attention_tails_bf16(gpu_ctx, t):
     gate(host(out), ref)
 
 
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+@pytest.mark.parametrize("jump", [12.0, 40.0])
+def test_attention_running_max_jump(gpu_ctx, dtype, jump):
+    # Key 530 (tile 5 of 96-key tiles) scores `jump` log2 units above what
+    # any query saw before, so the running max moves past the lazy-rescale
+    # threshold (2^8) in a later tile.  The kernel's cheap test (the tile's
+    # rounded row sum reaching 2^8) must catch it and rebuild the scores;
+    # at 40 the first-pass 16-bit P also overflows (f16) before the rebuild.
+    s, h, t, d = 1, 2, 700, 64
+    rng = np.random.default_rng(11)
+    u = rng.standard_normal(d).astype(np.float32)
+    u /= np.linalg.norm(u)
+    c = 0.125 * 1.4426950408889634
+    q = u * 8 + 0.3 * rng.standard_normal((s, h, t, d)).astype(np.float32)
+    k = 0.5 * rng.standard_normal((s, h, t, d)).astype(np.float32)
+    k[:, :, 530, :] = u * (jump / c / 8)
+    v = rng.standard_normal((s, h, t, d)).astype(np.float32)
+    q, k, v = (rounded(x, dtype) for x in (q, k, v))
+    ref = oracle.attention(q, k, v)
+    out = gpu_ctx.attention(dev(q, dtype), dev(k, dtype), dev(v, dtype))
+    gpu_ctx.sync()
+    gate(host(out), ref)
+
+
 def test_attention_f32_storage(gpu_ctx):
     # f32 callers: tensor cores see bf16-rounded q, k, v; out stays f32.
     s, h, t, d = 2, 2, 300, 64
@@ -80,11 +104,20 @@ def test_attention_f32_storage(gpu_ctx):
 
 # ---- fused QK-norm + RoPE (block.rs:136-148) --------------------------------
 
-def _fused_case(gpu_ctx, s, h, t, dtype, prefix, tpf, grid, seed, ln_random=True, rope=True):
+def _fused_case(gpu_ctx, s, h, t, dtype, prefix, tpf, grid, seed, ln_random=True, rope=True, ln_gain=None,
+                ln_shift=0.0, round_qk=False):
     d = 64
     rng = np.random.default_rng(seed)
     q, k, v = (rounded(rng.standard_normal((s, h, t, d), np.float32), dtype) for _ in range(3))
-    if ln_random:
+    if ln_gain is not None:
+        # Shared bias along one unit direction: it raises |q'| and |k'| (and
+        # so the kernel's score bound) while its q'.k' term is the same for
+        # every key and cancels in the softmax.
+        u = rng.standard_normal(d).astype(np.float32)
+        u /= np.linalg.norm(u)
+        qw = kw = np.full(d, ln_gain, np.float32)
+        qb = kb = (ln_shift * u).astype(np.float32)
+    elif ln_random:
         qw, qb, kw, kb = (rng.uniform(0.5, 1.5, d).astype(np.float32), rng.uniform(-0.2, 0.2, d).astype(np.float32),
                           rng.uniform(0.5, 1.5, d).astype(np.float32), rng.uniform(-0.2, 0.2, d).astype(np.float32))
     else:
@@ -96,6 +129,8 @@ def _fused_case(gpu_ctx, s, h, t, dtype, prefix, tpf, grid, seed, ln_random=True
         sin, cos = oracle.rope_tables(*grid)
     qn = oracle.qk_prep(q, qw, qb, eps, sin, cos, prefix, tpf)
     kn = oracle.qk_prep(k, kw, kb, eps, sin, cos, prefix, tpf)
+    if round_qk:  # the reference stores q', k' in the tensor dtype between its kernels
+        qn, kn = rounded(qn, dtype), rounded(kn, dtype)
     ref = oracle.attention(qn, kn, v)
     c = lambda a: torch.from_numpy(a).cuda()  # noqa: E731
     out = gpu_ctx.attention_fused(
@@ -127,6 +162,21 @@ def test_fused_global_multi_frame(gpu_ctx):
 
 def test_fused_no_rope(gpu_ctx):
     ours, ref = _fused_case(gpu_ctx, 1, 3, 500, "bf16", prefix=0, tpf=500, grid=(1, 1), seed=4, rope=False)
+    gate(ours, ref)
+
+
+@pytest.mark.parametrize("gain,shift", [(0.25, 0.0), (1.0, 0.0), (1.0, 14.0)])
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+def test_fused_score_bound_modes(gpu_ctx, dtype, gain, shift):
+    # The kernel bounds every score by max|q'| * max|k'| * scale * log2(e)
+    # (qk_prep records the norms; here |q'|, |k'| <= 8 * gain + shift).  A
+    # small bound selects the fixed-offset softmax (no running max): bf16 up
+    # to 48 (bounds 0.72 and 11.5 here), f16 up to 7 (0.72); the shifted
+    # case (bound 63) takes the running-max path in both types.  The oracle
+    # rounds q', k' to the dtype, as the reference's separate kernels store
+    # them.
+    ours, ref = _fused_case(gpu_ctx, 1, 4, 1374, dtype, prefix=5, tpf=1374, grid=(37, 37), seed=9, ln_gain=gain,
+                            ln_shift=shift, round_qk=True)
     gate(ours, ref)
 
 
