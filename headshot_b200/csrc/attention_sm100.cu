@@ -252,10 +252,9 @@ __device__ __forceinline__ void exp2_poly2(float x0, float x1, float& y0, float&
   y1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
 }
 
-// kFixed: every score is known to satisfy |s*c| <= m_fixed (Cauchy-Schwarz
-// on the stored q' and k' rows), so P = 2^(s*c - m_fixed) <= 1 for a fixed
-// offset: no row max, no rescale.  Used when m_fixed is small enough that
-// every P of a valid key stays far inside the 16-bit type's normal range.
+// kFixed: every score is known to be bounded (Cauchy-Schwarz on the stored
+// q' and k' rows), so P = 2^(s*c - m_fixed) for a fixed offset m_fixed
+// stays inside the 16-bit type's normal range: no row max, no rescale.
 template <typename E, bool kFixed>
 __device__ void softmax_role(const Args& a, Ctrl* ctl, uint32_t tmem, int warp, int lane, float m_fixed) {
   const int wg = warp >> 2;
@@ -452,11 +451,15 @@ __device__ void softmax_role(const Args& a, Ctrl* ctl, uint32_t tmem, int warp, 
   }
 }
 
-// Largest offset for the fixed-offset softmax: valid keys keep P >=
-// 2^(-2 * limit), inside the normal range with room to spare (bf16: 2^-96,
-// ~30 binades above what a masked key can round to; f16: 2^-14).
+// Fixed-offset softmax: with |s*c| <= B for every score, P = 2^(s*c - m)
+// lies in [2^(-B-m), 2^(B-m)].  bf16 (8 exponent bits): m = B, so P <= 1,
+// for B <= 48 (valid keys keep P >= 2^-96, ~30 binades above anything a
+// masked key can round to).  f16 (5 exponent bits): m = B - 15.5, so P <=
+// 2^15.5 < 65504 and P >= 2^(15.5 - 2B) >= 2^-12.5 (normal) for B <= 14.
 template <typename E>
-__host__ __device__ constexpr float fixed_offset_limit() { return Elem<E>::kBf16 ? 48.f : 7.f; }
+__host__ __device__ constexpr float fixed_offset_limit() { return Elem<E>::kBf16 ? 48.f : 14.f; }
+template <typename E>
+__host__ __device__ constexpr float fixed_offset_headroom() { return Elem<E>::kBf16 ? 0.f : 15.5f; }
 
 template <typename E>
 __device__ void softmax_dispatch(const Args& a, Ctrl* ctl, uint32_t tmem, int warp, int lane) {
@@ -468,7 +471,7 @@ __device__ void softmax_dispatch(const Args& a, Ctrl* ctl, uint32_t tmem, int wa
     bound = qn * kn * a.scale_log2 * 1.0009765625f + 1e-3f;
   }
   if (bound <= fixed_offset_limit<E>())
-    softmax_role<E, true>(a, ctl, tmem, warp, lane, bound);
+    softmax_role<E, true>(a, ctl, tmem, warp, lane, bound - fixed_offset_headroom<E>());
   else
     softmax_role<E, false>(a, ctl, tmem, warp, lane, 0.f);
 }

@@ -171,8 +171,8 @@ def test_fused_score_bound_modes(gpu_ctx, dtype, gain, shift):
     # The kernel bounds every score by max|q'| * max|k'| * scale * log2(e)
     # (qk_prep records the norms; here |q'|, |k'| <= 8 * gain + shift).  A
     # small bound selects the fixed-offset softmax (no running max): bf16 up
-    # to 48 (bounds 0.72 and 11.5 here), f16 up to 7 (0.72); the shifted
-    # case (bound 63) takes the running-max path in both types.  The oracle
+    # to 48, f16 up to 14 (bounds 0.72 and 11.5 here); the shifted case
+    # (bound 63) takes the running-max path in both types.  The oracle
     # rounds q', k' to the dtype, as the reference's separate kernels store
     # them.
     ours, ref = _fused_case(gpu_ctx, 1, 4, 1374, dtype, prefix=5, tpf=1374, grid=(37, 37), seed=9, ln_gain=gain,
