@@ -158,7 +158,8 @@ hs_status attention_impl(hs_ctx* ctx, const void* q, const void* k, const void* 
   {
     ProfScope prof(ctx, st, "attention");
     e = launch_attention_sm100(st, elem, use[0], use[1], use[2], out, code == kF32 ? kF32 : elem, S * H, T, T,
-                               scale, state, 0, ctx->d_status, ctx->d_sched, norm2, ctx_timeout_ns(ctx), &err);
+                               scale, state, 0, ctx->d_status, ctx->d_sched, norm2, false, ctx_timeout_ns(ctx),
+                               &err);
   }
   if (e != cudaSuccess) return fail(HS_ERR_CUDA, std::string(name) + ": " + (err.empty() ? cudaGetErrorString(e) : err));
   return HS_OK;

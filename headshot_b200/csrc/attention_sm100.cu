@@ -129,8 +129,11 @@ static_assert(kSmemBytes <= 232448, "shared memory per CTA");
 struct Args {
   void* out;
   // Max squared norms of the q' and k' rows (f32 bit patterns, set by
-  // qk_prep), or null.  Zeroed by the last CTA, ready for the next call.
+  // qk_prep), or null.  Zeroed by the last CTA, ready for the next call,
+  // unless shared: then they bound every launch that carries the same
+  // softmax state (ring steps), which may then use the fixed offset too.
   unsigned int* qk_norm2;
+  int norm2_shared;
   uint32_t t_q;      // query rows per sequence
   uint32_t t_kv;     // keys per sequence
   uint32_t n_kv;     // ceil(t_kv / kBN)
@@ -464,7 +467,7 @@ __host__ __device__ constexpr float fixed_offset_headroom() { return Elem<E>::kB
 template <typename E>
 __device__ void softmax_dispatch(const Args& a, Ctrl* ctl, uint32_t tmem, int warp, int lane) {
   float bound = INFINITY;
-  if (a.qk_norm2 && !a.st.load && !a.st.store) {
+  if (a.qk_norm2 && (a.norm2_shared || (!a.st.load && !a.st.store))) {
     const float qn = sqrtf(__uint_as_float(a.qk_norm2[0]));
     const float kn = sqrtf(__uint_as_float(a.qk_norm2[1]));
     // Margin for the f32 accumulation inside the tensor core.
@@ -732,7 +735,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (atomicAdd(&a.sched[1], 1u) == gridDim.x - 1) {
       atomicExch(&a.sched[0], 0u);
       atomicExch(&a.sched[1], 0u);
-      if (a.qk_norm2) {  // every CTA read the bounds at its start
+      if (a.qk_norm2 && !a.norm2_shared) {  // every CTA read the bounds at its start
         atomicExch(&a.qk_norm2[0], 0u);
         atomicExch(&a.qk_norm2[1], 0u);
       }
@@ -812,7 +815,8 @@ cudaError_t launch_typed(cudaStream_t stream, const CUtensorMap& mq, const CUten
 cudaError_t launch_attention_sm100(cudaStream_t stream, int elem, const void* q, const void* k, const void* v,
                                    void* out, int out_code, uint32_t sh, uint32_t t_q, uint32_t t_kv, float scale,
                                    const AttnState& st, uint32_t max_ctas, int* status, uint32_t* sched,
-                                   unsigned int* qk_norm2, uint64_t timeout_ns, std::string* err) {
+                                   unsigned int* qk_norm2, bool norm2_shared, uint64_t timeout_ns,
+                                   std::string* err) {
   if (t_q == 0 || sh == 0) return cudaSuccess;
   const bool bf16 = elem == kBF16;
   CUtensorMap mq, mk, mv;
@@ -837,6 +841,7 @@ cudaError_t launch_attention_sm100(cudaStream_t stream, int elem, const void* q,
   a.status = status;
   a.sched = sched;
   a.qk_norm2 = qk_norm2;
+  a.norm2_shared = norm2_shared ? 1 : 0;
   a.timeout_ns = timeout_ns;
   uint32_t ctas = max_ctas ? max_ctas : static_cast<uint32_t>(sm_count_of_current_device());
   if (ctas > a.n_items) ctas = a.n_items;

@@ -51,11 +51,13 @@ struct AttnState {
 // `qk_norm2` (2 x u32 or null): the max squared row norms of q and k as
 // qk_prep recorded them; when they bound every score tightly enough the
 // softmax uses a fixed offset instead of a running max.  Zeroed by the
-// kernel.
+// kernel unless `norm2_shared`: then the caller guarantees they bound every
+// launch that carries the same state `st` (all ring steps) and resets them.
 cudaError_t launch_attention_sm100(cudaStream_t stream, int elem, const void* q, const void* k, const void* v,
                                    void* out, int out_code, uint32_t sh, uint32_t t_q, uint32_t t_kv, float scale,
                                    const AttnState& st, uint32_t max_ctas, int* status, uint32_t* sched,
-                                   unsigned int* qk_norm2, uint64_t timeout_ns, std::string* err);
+                                   unsigned int* qk_norm2, bool norm2_shared, uint64_t timeout_ns,
+                                   std::string* err);
 
 // Row prep for K (and for casts): out = RoPE(LN(x)) in `out_code` storage.
 cudaError_t launch_qk_prep(cudaStream_t stream, const void* x, int in_code, void* out, int out_code,

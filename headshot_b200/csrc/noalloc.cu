@@ -163,7 +163,7 @@ extern "C" hs_status hs_attention_fused_noalloc(void* stream, int* status, const
   std::string err;
   hs::AttnState state{};
   e = hs::launch_attention_sm100(st, code, q_use, k_use, v, out, code, S * H, T, T, scale, state, 0, status_word,
-                                 p.sched, (ln || rope) ? p.sched + 2 : nullptr, kNoAllocTimeoutNs, &err);
+                                 p.sched, (ln || rope) ? p.sched + 2 : nullptr, false, kNoAllocTimeoutNs, &err);
   if (e != cudaSuccess)
     return hs::abi_fail(HS_ERR_CUDA, std::string(name) + ": " + (err.empty() ? cudaGetErrorString(e) : err));
   return HS_OK;

@@ -40,6 +40,8 @@ struct NcclApi {
   ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
   ncclResult_t (*Send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
   ncclResult_t (*Recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                            cudaStream_t) = nullptr;
   ncclResult_t (*GroupStart)() = nullptr;
   ncclResult_t (*GroupEnd)() = nullptr;
   const char* (*GetErrorString)(ncclResult_t) = nullptr;
@@ -67,6 +69,7 @@ NcclApi& nccl() {
     sym(api.CommGetAsyncError, "ncclCommGetAsyncError");
     sym(api.Send, "ncclSend");
     sym(api.Recv, "ncclRecv");
+    sym(api.AllReduce, "ncclAllReduce");
     sym(api.GroupStart, "ncclGroupStart");
     sym(api.GroupEnd, "ncclGroupEnd");
     sym(api.GetErrorString, "ncclGetErrorString");
@@ -106,6 +109,10 @@ struct hs_ring {
   cudaEvent_t ev_recv[2] = {nullptr, nullptr};
   cudaEvent_t ev_compute[2] = {nullptr, nullptr};
   cudaEvent_t ev_done = nullptr;
+  cudaEvent_t ev_bound = nullptr;  // the all-ranks score bound is ready
+  // Largest squared q' and k' row norms over all ranks (f32 bit patterns):
+  // one bound on every score of every ring step.
+  unsigned int* norm2 = nullptr;
   void* buf[2] = {nullptr, nullptr};
   size_t buf_bytes = 0;
   // Per query row of this rank's shard: the normalised/rotated q (64 x 16-bit),
@@ -170,8 +177,9 @@ hs_status hs_ring_create(hs_ctx* ctx, int rank, int world, const void* id, hs_ri
   }
   cudaError_t e = cudaStreamCreateWithFlags(&ring->comm_stream, cudaStreamNonBlocking);
   for (cudaEvent_t* ev : {&ring->ev_block0, &ring->ev_recv[0], &ring->ev_recv[1], &ring->ev_compute[0],
-                          &ring->ev_compute[1], &ring->ev_done})
+                          &ring->ev_compute[1], &ring->ev_done, &ring->ev_bound})
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(ev, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaMalloc(&ring->norm2, 2 * sizeof(unsigned int));
   if (e != cudaSuccess) {
     n.CommDestroy(ring->comm);
     delete ring;
@@ -198,8 +206,9 @@ hs_status hs_ring_destroy(hs_ring* ring) {
   for (void* b : ring->buf)
     if (b) cudaFree(b);
   if (ring->state) cudaFree(ring->state);
+  if (ring->norm2) cudaFree(ring->norm2);
   for (cudaEvent_t ev : {ring->ev_block0, ring->ev_recv[0], ring->ev_recv[1], ring->ev_compute[0],
-                         ring->ev_compute[1], ring->ev_done})
+                         ring->ev_compute[1], ring->ev_done, ring->ev_bound})
     if (ev) cudaEventDestroy(ev);
   if (ring->comm_stream) cudaStreamDestroy(ring->comm_stream);
   delete ring;
@@ -286,20 +295,27 @@ hs_status hs_ring_attention_fused(hs_ring* ring, const void* q, const void* k, c
                               k_norm_b, eps, rope_sin, rope_cos, rope_rows, prefix, tokens_per_frame);
   }
 
-  // Block 0 = this rank's [K' | V] in buf[0].
+  // Block 0 = this rank's [K' | V] in buf[0], and this rank's Q'.  The
+  // preps also record the largest q' and k' row norms; an all-ranks max of
+  // those bounds every score of every step (fixed-offset softmax).
+  const bool bounded = ln || rope;
   uint8_t* b0 = static_cast<uint8_t*>(ring->buf[0]);
+  const void* q_use = q;
+  if (bounded) {
+    e = cudaMemsetAsync(ring->norm2, 0, 2 * sizeof(unsigned int), st);
+    if (e != cudaSuccess) return hs::abi_cuda_fail(e, "ring bound reset");
+    kp.norm2_max = ring->norm2 + 1;
+    qp.norm2_max = ring->norm2;
+  }
   {
     hs::ProfScope prof(ctx, st, "qk_prep");
-    e = (ln || rope) ? hs::launch_qk_prep(st, k, code, b0, code, rows, tr, kp)
-                     : cudaMemcpyAsync(b0, k, rows * row_bytes, cudaMemcpyDeviceToDevice, st);
+    e = bounded ? hs::launch_qk_prep(st, k, code, b0, code, rows, tr, kp)
+                : cudaMemcpyAsync(b0, k, rows * row_bytes, cudaMemcpyDeviceToDevice, st);
   }
   if (e != cudaSuccess) return hs::abi_cuda_fail(e, "ring K' prep");
   e = cudaMemcpyAsync(b0 + rows * row_bytes, v, rows * row_bytes, cudaMemcpyDeviceToDevice, st);
   if (e != cudaSuccess) return hs::abi_cuda_fail(e, "ring V copy");
-  cudaEventRecord(ring->ev_block0, st);
-
-  const void* q_use = q;
-  if (ln || rope) {
+  if (bounded) {
     {
       hs::ProfScope prof(ctx, st, "qk_prep");
       e = hs::launch_qk_prep(st, q, code, ring->state, code, rows, tr, qp);
@@ -307,6 +323,15 @@ hs_status hs_ring_attention_fused(hs_ring* ring, const void* q, const void* k, c
     if (e != cudaSuccess) return hs::abi_cuda_fail(e, "ring Q' prep");
     q_use = ring->state;
   }
+  cudaEventRecord(ring->ev_block0, st);
+  if (bounded) {
+    cudaStreamWaitEvent(cs, ring->ev_block0, 0);
+    ncclResult_t nr = n.AllReduce(ring->norm2, ring->norm2, 2, ncclUint32, ncclMax, ring->comm, cs);
+    if (nr != ncclSuccess) return nccl_fail(nr, "ring bound all-reduce");
+    cudaEventRecord(ring->ev_bound, cs);
+    cudaStreamWaitEvent(st, ring->ev_bound, 0);
+  }
+
   hs::AttnState state{};
   float* state_f = reinterpret_cast<float*>(ring->state + rows * row_bytes);
   state.o = state_f;
@@ -341,7 +366,7 @@ hs_status hs_ring_attention_fused(hs_ring* ring, const void* q, const void* k, c
       hs::ProfScope prof(ctx, st, "attention");
       e = hs::launch_attention_sm100(st, code, q_use, cur, cur + static_cast<size_t>(H) * src_len * row_bytes, out,
                                      code, H, tr, src_len, scale, state, 0, ctx->d_status, ctx->d_sched,
-                                     nullptr, hs::ctx_timeout_ns(ctx), &err);
+                                     bounded ? ring->norm2 : nullptr, true, hs::ctx_timeout_ns(ctx), &err);
     }
     if (e != cudaSuccess)
       return hs::abi_fail(HS_ERR_CUDA, std::string(name) + ": " + (err.empty() ? cudaGetErrorString(e) : err));

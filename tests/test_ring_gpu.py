@@ -33,7 +33,7 @@ def _gpus() -> int:
     return torch.cuda.device_count() if torch.cuda.is_available() else 0
 
 
-@pytest.mark.parametrize("world,T,fused,dtype", [(2, 2748, True, "bf16"), (2, 1001, False, "f16")])
+@pytest.mark.parametrize("world,T,fused,dtype", [(2, 2748, True, "bf16"), (2, 2748, True, "f16"), (2, 1001, False, "f16")])
 def test_ring_matches_oracle(tmp_path, world, T, fused, dtype):
     if _gpus() < world:
         pytest.skip(f"needs {world} GPUs")
