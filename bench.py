@@ -280,18 +280,30 @@ def run_ours(args, wl: dict, rank: int, world: int, local: int) -> dict | None:
     value = flops_total / (ms_per_step / 1e3) / 1e12
 
     # ---- end to end through the C ABI: pinned host in, host out -------
+    # Every step copies its q, k, v from pinned host memory (hs_memcpy_h2d) and
+    # its output back (hs_memcpy_d2h).  Serial: copies and compute in one
+    # stream.  Pipelined (the reported value): two device buffer sets; step
+    # i+1's inputs upload on one copy stream and step i-1's output downloads
+    # on another while step i computes, as a serving loop would run it.  All
+    # copies of all timed steps lie inside the timed region.
     qh, kh, vh = (x.cpu().pin_memory() for x in (q, k, v))
-    oh = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-    e2e_steps = max(1, min(args.steps, 5))
+    oh = [torch.empty(out.shape, dtype=out.dtype).pin_memory() for _ in range(2)]
+    e2e_steps = max(2, min(args.steps, 6))
 
-    def e2e_step():
+    def run_step(qq, kk, vv, oo):
+        if session is None:
+            ctx.attention_fused(qq, kk, vv, qk_norm=norm, rope=rope, out=oo)
+        else:
+            session.attention_fused(qq, kk, vv, oo, T_total=T, qk_norm=norm, rope=rope)
+
+    def e2e_serial():
         ctx.upload(q, qh)
         ctx.upload(k, kh)
         ctx.upload(v, vh)
-        step()
-        ctx.download(oh, out)
+        run_step(q, k, v, out)
+        ctx.download(oh[0], out)
 
-    e2e_step()
+    e2e_serial()
     torch.cuda.synchronize(dev)
     barrier(world)
     torch.cuda.synchronize(dev)
@@ -299,14 +311,62 @@ def run_ours(args, wl: dict, rank: int, world: int, local: int) -> dict | None:
     f1 = torch.cuda.Event(enable_timing=True)
     f0.record(stream)
     for _ in range(e2e_steps):
-        e2e_step()
+        e2e_serial()
+    f1.record(stream)
+    torch.cuda.synchronize(dev)
+    ctx.sync()
+    serial_ms = max_over_ranks(f0.elapsed_time(f1) / e2e_steps, world)
+
+    sets = [(q, k, v, out), tuple(torch.empty_like(x) for x in (q, k, v, out))]
+    up_stream, down_stream = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_done = [torch.cuda.Event() for _ in range(2)]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
+
+    def upload_set(i):
+        b = i % 2
+        with torch.cuda.stream(up_stream):
+            if i >= 2:
+                up_stream.wait_event(ev_done[b])  # step i-2 has finished reading this set
+            for dst, src in zip(sets[b][:3], (qh, kh, vh)):
+                ctx.upload(dst, src)
+            ev_in[b].record(up_stream)
+
+    def pipelined(n):
+        upload_set(0)
+        for i in range(n):
+            b = i % 2
+            if i + 1 < n:
+                upload_set(i + 1)
+            stream.wait_event(ev_in[b])
+            if i >= 2:
+                stream.wait_event(ev_out[b])  # step i-2's output has left this set's out buffer
+            run_step(*sets[b])
+            ev_done[b].record(stream)
+            with torch.cuda.stream(down_stream):
+                down_stream.wait_event(ev_done[b])
+                ctx.download(oh[b], sets[b][3])
+                ev_out[b].record(down_stream)
+        stream.wait_stream(down_stream)
+        stream.wait_stream(up_stream)
+
+    pipelined(2)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    f0.record(stream)
+    up_stream.wait_event(f0)
+    down_stream.wait_event(f0)
+    pipelined(e2e_steps)
     f1.record(stream)
     torch.cuda.synchronize(dev)
     ctx.sync()
     e2e_ms = max_over_ranks(f0.elapsed_time(f1) / e2e_steps, world)
     e2e_value = flops_total / (e2e_ms / 1e3) / 1e12
+    serial_value = flops_total / (serial_ms / 1e3) / 1e12
     h2d = 3 * q.numel() * q.element_size() * world
     d2h = out.numel() * out.element_size() * world
+    del sets
 
     # ---- roofline of the dominant kernel (attention), live events ----
     peaks = measured_peaks()
@@ -352,7 +412,9 @@ def run_ours(args, wl: dict, rank: int, world: int, local: int) -> dict | None:
             "roofline": roofline,
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3), "steps": e2e_steps},
+                    "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3), "steps": e2e_steps,
+                    "mode": "pipelined: step i+1's uploads and step i-1's download overlap step i's compute",
+                    "serial_value": round(serial_value, 2), "serial_ms_per_step": round(serial_ms, 3)},
             "gpu_launches": int(all_n) * world,
             "clocks": clocks,
         }

@@ -1,10 +1,12 @@
 // ops.cu — memory-bound companions of the attention op:
-//   qk_prep      K' = RoPE(LN(K)) (and plain 16-bit casts), one pass over HBM
+//   qk_prep      Q' and K' = RoPE(LN(x)) (and plain 16-bit casts), one pass over HBM
 //   layernorm    GpuContext::layernorm  (src/engine/ops.rs:130-153, shaders/layernorm.wesl)
 //   rope_apply   GpuContext::rope_apply (src/engine/ops.rs:202-223, shaders/rope_apply.wesl)
 //   split_heads  GpuContext::split_heads (src/engine/ops.rs:185-200, shaders/split_heads.wesl)
 //   attn_merge   GpuContext::attn_merge  (src/engine/ops.rs:255-267, shaders/attn_merge.wesl)
 // Storage may be f32, f16 or bf16; all arithmetic is f32.
+#include <type_traits>
+
 #include "hs_internal.h"
 #include "hs_ptx.cuh"
 
@@ -84,72 +86,140 @@ __device__ __forceinline__ void store8(T* p, const float (&v)[8]) {
 
 constexpr int kPrepTokens = 32;     // tokens per block (8 threads per 64-wide row)
 constexpr int kPrepSeqPerBlock = 16;  // sequences (s, h) a block sweeps with one staged table slice
-constexpr int kPrepBatch = 4;         // of those, rows loaded back to back by one thread
 
-// K' = RoPE(LN(x)) over (SH, T, 64).  A block owns kPrepTokens consecutive
-// tokens of up to kPrepSeqPerBlock sequences: the sin/cos rows of its tokens
-// are staged in shared memory once and reused for every sequence (the table
-// row depends on the token only), which keeps the table reads from costing
-// more L2 traffic than the rows themselves.  Eight threads per row; thread g
-// holds elements [8g, 8g+8) and the RoPE partner of element i < 32 (i + 32)
-// sits in thread g ^ 4.
+// One thread's 8 elements of a 64-wide row: [4g, 4g+4) and their RoPE
+// partners [32+4g, 36+4g), raw as stored (8 bytes each half for 16-bit, 16
+// for f32).
+template <typename In>
+struct RawHalves {
+  static constexpr bool kF32 = sizeof(In) == 4;
+  using Half = typename std::conditional<kF32, uint4, uint2>::type;
+  Half lo, hi;
+  __device__ __forceinline__ void load(const In* row, int g) {
+    lo = __ldg(reinterpret_cast<const Half*>(row + 4 * g));
+    hi = __ldg(reinterpret_cast<const Half*>(row + 32 + 4 * g));
+  }
+  __device__ __forceinline__ void zero() {
+    if constexpr (kF32) {
+      lo = hi = make_uint4(0u, 0u, 0u, 0u);
+    } else {
+      lo = hi = make_uint2(0u, 0u);
+    }
+  }
+  // v[0..3] = elements 4g..4g+3, v[4..7] = elements 32+4g..35+4g.
+  __device__ __forceinline__ void to_float(float (&v)[8]) const {
+    if constexpr (kF32) {
+      v[0] = __uint_as_float(lo.x); v[1] = __uint_as_float(lo.y); v[2] = __uint_as_float(lo.z);
+      v[3] = __uint_as_float(lo.w); v[4] = __uint_as_float(hi.x); v[5] = __uint_as_float(hi.y);
+      v[6] = __uint_as_float(hi.z); v[7] = __uint_as_float(hi.w);
+    } else {
+      const uint32_t w[4] = {lo.x, lo.y, hi.x, hi.y};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = Elem<In>::unpack2(w[i]);
+        v[2 * i] = f.x;
+        v[2 * i + 1] = f.y;
+      }
+    }
+  }
+};
+
+// Stores v (layout of RawHalves::to_float) at row + 4g and row + 32 + 4g and
+// returns the squared norm of the values as stored (after rounding).
+template <typename Out>
+__device__ __forceinline__ float store_halves(Out* row, int g, const float (&v)[8]) {
+  float n2 = 0.f;
+  if constexpr (sizeof(Out) == 4) {
+    *reinterpret_cast<float4*>(row + 4 * g) = make_float4(v[0], v[1], v[2], v[3]);
+    *reinterpret_cast<float4*>(row + 32 + 4 * g) = make_float4(v[4], v[5], v[6], v[7]);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) n2 = fmaf(v[i], v[i], n2);
+  } else {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      w[i] = Elem<Out>::pack2(v[2 * i], v[2 * i + 1]);
+      const float2 r = Elem<Out>::unpack2(w[i]);
+      n2 = fmaf(r.x, r.x, n2);
+      n2 = fmaf(r.y, r.y, n2);
+    }
+    *reinterpret_cast<uint2*>(row + 4 * g) = make_uint2(w[0], w[1]);
+    *reinterpret_cast<uint2*>(row + 32 + 4 * g) = make_uint2(w[2], w[3]);
+  }
+  return n2;
+}
+
+// Q' or K' = RoPE(LN(x)) over (SH, T, 64).  A block owns kPrepTokens
+// consecutive tokens of up to kPrepSeqPerBlock sequences.  Eight threads per
+// row; thread g holds elements [4g, 4g+4) and their rotate-half partners
+// [32+4g, 36+4g), so RoPE needs no exchange between threads, and the table
+// values of its 8 columns, which depend on the token only, are loaded once
+// and reused for every sequence.  Each thread issues the loads of all its
+// rows before any arithmetic, so enough bytes are in flight for HBM.
 template <typename In, typename Out>
 __global__ void __launch_bounds__(256) qk_prep_kernel(const In* __restrict__ x, Out* __restrict__ out, uint32_t sh,
                                                       uint32_t t, QkPrologue p) {
-  __shared__ float sin_s[kPrepTokens][64];
-  __shared__ float cos_s[kPrepTokens][64];
-  __shared__ int rot_s[kPrepTokens];
+  constexpr int kRows = sizeof(In) == 4 ? kPrepSeqPerBlock / 2 : kPrepSeqPerBlock;  // rows per pass
   const int lt = threadIdx.x >> 3;  // token within the block
   const int g = threadIdx.x & 7;
   const uint32_t tok = blockIdx.x * kPrepTokens + lt;
   const bool tok_ok = tok < t;
-  if (p.rope) {
-    if (threadIdx.x < kPrepTokens) {
-      const uint32_t tk = blockIdx.x * kPrepTokens + threadIdx.x;
-      const uint32_t ft = (tk + p.pos_offset) % p.tokens_per_frame;
-      rot_s[threadIdx.x] = (tk < t && ft >= p.prefix) ? static_cast<int>(ft - p.prefix) : -1;
-    }
-    __syncthreads();
-    // Scalar loads: the tables come through the C ABI with only 4-byte alignment promised.
-    for (int i = threadIdx.x; i < kPrepTokens * 64; i += blockDim.x) {
-      const int tt = i >> 6, c = i & 63;
-      const int r = rot_s[tt];
-      float sv = 0.f, cv = 1.f;
-      if (r >= 0) {
-        sv = __ldg(p.sin_t + static_cast<uint64_t>(r) * 64 + c);
-        cv = __ldg(p.cos_t + static_cast<uint64_t>(r) * 64 + c);
+  const uint32_t seq0 = blockIdx.y * kPrepSeqPerBlock;
+  const uint32_t seq_end = min(sh, seq0 + kPrepSeqPerBlock);
+  auto row_at = [&](uint32_t q) { return (static_cast<uint64_t>(q) * t + tok) * 64; };
+
+  RawHalves<In> raw[kRows];
+#pragma unroll
+  for (int u = 0; u < kRows; ++u) {
+    if (tok_ok && seq0 + u < seq_end) raw[u].load(x + row_at(seq0 + u), g);
+    else raw[u].zero();
+  }
+  // This thread's table columns (pass-through rows: sin 0, cos 1).  Scalar
+  // loads: the tables come through the C ABI with only 4-byte alignment.
+  float sn[8], cs[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    sn[i] = 0.f;
+    cs[i] = 1.f;
+  }
+  if (p.rope && tok_ok) {
+    const uint32_t ft = (tok + p.pos_offset) % p.tokens_per_frame;
+    if (ft >= p.prefix) {
+      const uint64_t r = static_cast<uint64_t>(ft - p.prefix) * 64;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        sn[i] = __ldg(p.sin_t + r + 4 * g + i);
+        sn[4 + i] = __ldg(p.sin_t + r + 32 + 4 * g + i);
+        cs[i] = __ldg(p.cos_t + r + 4 * g + i);
+        cs[4 + i] = __ldg(p.cos_t + r + 32 + 4 * g + i);
       }
-      sin_s[tt][c] = sv;
-      cos_s[tt][c] = cv;
     }
-    __syncthreads();
   }
   float w[8], bb[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    w[i] = p.ln ? __ldg(p.ln_w + 8 * g + i) : 1.f;
-    bb[i] = p.ln ? __ldg(p.ln_b + 8 * g + i) : 0.f;
+  for (int i = 0; i < 4; ++i) {
+    w[i] = p.ln ? __ldg(p.ln_w + 4 * g + i) : 1.f;
+    w[4 + i] = p.ln ? __ldg(p.ln_w + 32 + 4 * g + i) : 1.f;
+    bb[i] = p.ln ? __ldg(p.ln_b + 4 * g + i) : 0.f;
+    bb[4 + i] = p.ln ? __ldg(p.ln_b + 32 + 4 * g + i) : 0.f;
   }
-  const uint32_t seq_end = min(sh, (blockIdx.y + 1) * kPrepSeqPerBlock);
   float n2_max = 0.f;
-  // kPrepBatch rows in flight per thread: their loads are issued together.
-  for (uint32_t q0 = blockIdx.y * kPrepSeqPerBlock; q0 < seq_end; q0 += kPrepBatch) {
-    float v[kPrepBatch][8];
+  for (uint32_t q0 = seq0; q0 < seq_end; q0 += kRows) {
+    if (q0 != seq0) {  // f32 storage: a second pass over the block's sequences
 #pragma unroll
-    for (int u = 0; u < kPrepBatch; ++u) {
-      if (tok_ok && q0 + u < seq_end) {
-        load8(x + (static_cast<uint64_t>(q0 + u) * t + tok) * 64 + 8 * g, v[u]);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) v[u][i] = 0.f;
+      for (int u = 0; u < kRows; ++u) {
+        if (tok_ok && q0 + u < seq_end) raw[u].load(x + row_at(q0 + u), g);
+        else raw[u].zero();
       }
     }
 #pragma unroll
-    for (int u = 0; u < kPrepBatch; ++u) {
+    for (int u = 0; u < kRows; ++u) {
+      float v[8];
+      raw[u].to_float(v);
       if (p.ln) {
         float sm = 0.f;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) sm += v[u][i];
+        for (int i = 0; i < 8; ++i) sm += v[i];
         sm += __shfl_xor_sync(0xffffffffu, sm, 1);
         sm += __shfl_xor_sync(0xffffffffu, sm, 2);
         sm += __shfl_xor_sync(0xffffffffu, sm, 4);
@@ -157,7 +227,7 @@ __global__ void __launch_bounds__(256) qk_prep_kernel(const In* __restrict__ x, 
         float sq = 0.f;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const float d = v[u][i] - mu;
+          const float d = v[i] - mu;
           sq = fmaf(d, d, sq);
         }
         sq += __shfl_xor_sync(0xffffffffu, sq, 1);
@@ -165,24 +235,21 @@ __global__ void __launch_bounds__(256) qk_prep_kernel(const In* __restrict__ x, 
         sq += __shfl_xor_sync(0xffffffffu, sq, 4);
         const float inv = rsqrtf(sq * (1.0f / 64) + p.eps);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) v[u][i] = (v[u][i] - mu) * inv * w[i] + bb[i];
+        for (int i = 0; i < 8; ++i) v[i] = (v[i] - mu) * inv * w[i] + bb[i];
       }
       if (p.rope) {
-        float pv[8];
+        // lower half: x*cos - x[i+32]*sin ; upper half: x*cos + x[i-32]*sin
 #pragma unroll
-        for (int i = 0; i < 8; ++i) pv[i] = __shfl_xor_sync(0xffffffffu, v[u][i], 4);
-        // Pass-through rows hold sin 0 / cos 1, so every row takes the same path.
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float sn = sin_s[lt][8 * g + i], cs = cos_s[lt][8 * g + i];
-          // lower half: x*cos - x[i+32]*sin ; upper half: x*cos + x[i-32]*sin
-          v[u][i] = g < 4 ? v[u][i] * cs - pv[i] * sn : v[u][i] * cs + pv[i] * sn;
+        for (int i = 0; i < 4; ++i) {
+          const float lo = v[i], hi = v[4 + i];
+          v[i] = lo * cs[i] - hi * sn[i];
+          v[4 + i] = hi * cs[4 + i] + lo * sn[4 + i];
         }
       }
       const bool row_ok = tok_ok && q0 + u < seq_end;
-      if (row_ok) store8(out + (static_cast<uint64_t>(q0 + u) * t + tok) * 64 + 8 * g, v[u]);
+      float n2 = 0.f;
+      if (row_ok) n2 = store_halves(out + row_at(q0 + u), g, v);
       if (p.norm2_max) {  // uniform branch: the row's 8 lanes add their parts
-        float n2 = row_ok ? stored_norm2<Out>(v[u]) : 0.f;
         n2 += __shfl_xor_sync(0xffffffffu, n2, 1);
         n2 += __shfl_xor_sync(0xffffffffu, n2, 2);
         n2 += __shfl_xor_sync(0xffffffffu, n2, 4);
