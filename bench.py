@@ -42,6 +42,13 @@ WORKLOADS = {
     "frame": dict(S=200, H=16, frames=1, T_f=1374, dtype="f16", seed=2, prefix=5, grid=(37, 37), eps=1e-6,
                   name="batched frame attention, 200 frames x 1374 tokens, 16 heads x 64, fp16, "
                        "fused QK-LayerNorm + 2D RoPE (37x37, 5 special tokens)"),
+    # Same work as "frame" on the layout Block::forward hands over: q, k, v are the
+    # (S*T, H*D) projection outputs and the output is the merged (S*T, H*D) tensor
+    # (split_heads, QK-norm, RoPE, attention and attn_merge in one call).
+    "frame_block": dict(S=200, H=16, frames=1, T_f=1374, dtype="f16", seed=2, prefix=5, grid=(37, 37), eps=1e-6,
+                        layout="block",
+                        name="batched frame attention on the projection layout (S*T, H*D) in and merged out, "
+                             "200 frames x 1374 tokens, 16 heads x 64, fp16, fused QK-LayerNorm + 2D RoPE"),
 }
 
 
@@ -218,9 +225,10 @@ def run_ours(args, wl: dict, rank: int, world: int, local: int) -> dict | None:
     b = torch.zeros(64, device=dev)
     norm = QkNorm(w, b, w, b, wl["eps"])
 
+    block = wl.get("layout") == "block"
     if S > 1:  # frame attention: frames sharded across ranks, no communication
         s0, s1 = shard_bounds(S, world, rank)
-        shape = (s1 - s0, H, T, 64)
+        shape = ((s1 - s0) * T, H * 64) if block else (s1 - s0, H, T, 64)
         flops_rank = 4.0 * (s1 - s0) * H * T * T * 64
         flops_total = 4.0 * S * H * T * T * 64
         session = None
@@ -240,7 +248,10 @@ def run_ours(args, wl: dict, rank: int, world: int, local: int) -> dict | None:
     out = torch.empty_like(q)
     rope = Rope(sin_d, cos_d, wl["prefix"], T_f)
 
-    if session is None:
+    if block:
+        def step():
+            ctx.attention_block(q, k, v, s1 - s0, T, H, qk_norm=norm, rope=rope, out=out)
+    elif session is None:
         def step():
             ctx.attention_fused(q, k, v, qk_norm=norm, rope=rope, out=out)
     else:
@@ -291,7 +302,9 @@ def run_ours(args, wl: dict, rank: int, world: int, local: int) -> dict | None:
     e2e_steps = max(2, min(args.steps, 6))
 
     def run_step(qq, kk, vv, oo):
-        if session is None:
+        if block:
+            ctx.attention_block(qq, kk, vv, s1 - s0, T, H, qk_norm=norm, rope=rope, out=oo)
+        elif session is None:
             ctx.attention_fused(qq, kk, vv, qk_norm=norm, rope=rope, out=oo)
         else:
             session.attention_fused(qq, kk, vv, oo, T_total=T, qk_norm=norm, rope=rope)

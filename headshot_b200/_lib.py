@@ -65,6 +65,8 @@ SIGNATURES = {
     "hs_attention": (_i, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _i, _f32]),
     "hs_attention_fused": (_i, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _i, _f32, _vp, _vp, _vp, _vp, _f32,
                                 _vp, _vp, _u32, _u32, _u32]),
+    "hs_attention_block_fused": (_i, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _i, _f32, _vp, _vp, _vp,
+                                      _vp, _f32, _vp, _vp, _u32, _u32, _u32]),
     "hs_layernorm": (_i, [_vp, _vp, _vp, _vp, _vp, _u64, _u32, _f32, _i]),
     "hs_rope_apply": (_i, [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _u32, _i]),
     "hs_split_heads": (_i, [_vp, _vp, _vp, _u32, _u32, _u32, _u32, _i]),

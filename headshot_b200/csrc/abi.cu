@@ -95,9 +95,11 @@ ProfScope::~ProfScope() {
 }
 
 // Shared validation + dispatch of the attention family.
+// `merged`: q, k, v are (S*T, H*D) projection outputs and out is the
+// (S*T, H*D) merged attention output; otherwise all four are (S, H, T, D).
 hs_status attention_impl(hs_ctx* ctx, const void* q, const void* k, const void* v, void* out, uint32_t S, uint32_t H,
                          uint32_t T, uint32_t D, hs_dtype dtype, float scale, const QkPrologue& qp,
-                         const QkPrologue& kp, const char* name) {
+                         const QkPrologue& kp, const char* name, bool merged = false) {
   if (!ctx) return fail(HS_ERR_INVALID, std::string(name) + ": null context");
   if (!valid_dtype(dtype)) return fail(HS_ERR_INVALID, std::string(name) + ": unknown dtype");
   const uint64_t n = static_cast<uint64_t>(S) * H * T * D;
@@ -130,7 +132,10 @@ hs_status attention_impl(hs_ctx* ctx, const void* q, const void* k, const void* 
     hs_status s = ctx_scratch(ctx, need, &scratch);
     if (s != HS_OK) return s;
   }
+  const RowLayout head_major = RowLayout::head_major(H, T);
+  const RowLayout given = merged ? RowLayout::token_major(H, T, static_cast<uint64_t>(H) * 64) : head_major;
   const void* use[3] = {q, k, v};
+  RowLayout lay[3] = {given, given, given};
   const bool direct[3] = {q_direct, k_direct, v_direct};
   // When both q and k pass through qk_prep it also records their largest
   // row norms, which let the attention kernel bound every score.
@@ -147,24 +152,71 @@ hs_status attention_impl(hs_ctx* ctx, const void* q, const void* k, const void* 
     if (direct[i]) continue;
     {
       ProfScope prof(ctx, st, "qk_prep");
-      e = launch_qk_prep(st, use[i], code, cursor, elem, rows, T, *pro[i]);
+      e = launch_qk_prep(st, use[i], code, given, cursor, elem, S, H, T, *pro[i]);
     }
     if (e != cudaSuccess) return cuda_fail(e, what[i]);
     use[i] = cursor;
+    lay[i] = head_major;
     cursor += tile_bytes;
   }
   std::string err;
   AttnState state{};
   {
     ProfScope prof(ctx, st, "attention");
-    e = launch_attention_sm100(st, elem, use[0], use[1], use[2], out, code == kF32 ? kF32 : elem, S * H, T, T,
-                               scale, state, 0, ctx->d_status, ctx->d_sched, norm2, false, ctx_timeout_ns(ctx),
-                               &err);
+    AttnIO io;
+    io.q = use[0];
+    io.lq = lay[0];
+    io.k = use[1];
+    io.lk = lay[1];
+    io.v = use[2];
+    io.lv = lay[2];
+    io.out = out;
+    io.lo = given;
+    io.out_code = code == kF32 ? kF32 : elem;
+    e = launch_attention_sm100(st, elem, io, S, H, T, T, scale, state, 0, ctx->d_status, ctx->d_sched, norm2, false,
+                               ctx_timeout_ns(ctx), &err);
   }
   if (e != cudaSuccess) return fail(HS_ERR_CUDA, std::string(name) + ": " + (err.empty() ? cudaGetErrorString(e) : err));
   return HS_OK;
 }
 
+}  // namespace hs
+
+namespace hs {
+// QK-norm + RoPE arguments of the fused entry points, validated.
+hs_status fused_prologues(const char* name, uint32_t T, const float* q_norm_w, const float* q_norm_b,
+                          const float* k_norm_w, const float* k_norm_b, float eps, const float* rope_sin,
+                          const float* rope_cos, uint32_t rope_rows, uint32_t prefix, uint32_t tokens_per_frame,
+                          QkPrologue* qp, QkPrologue* kp) {
+  const bool ln = q_norm_w != nullptr;
+  if (ln != (k_norm_w != nullptr) || (ln && (!q_norm_b || !k_norm_b)))
+    return fail(HS_ERR_INVALID, std::string(name) + ": QK-norm needs all of q/k weight and bias, or none");
+  const bool rope = rope_sin != nullptr;
+  if (rope && !rope_cos) return fail(HS_ERR_INVALID, std::string(name) + ": rope_cos missing");
+  const uint32_t tpf = tokens_per_frame ? tokens_per_frame : T;
+  if (rope) {
+    if (prefix > tpf) return fail(HS_ERR_INVALID, std::string(name) + ": prefix > tokens_per_frame");
+    if (static_cast<uint64_t>(rope_rows) < static_cast<uint64_t>(tpf - prefix))
+      return fail(HS_ERR_INVALID, std::string(name) + ": rope tables have " + std::to_string(rope_rows) +
+                                      " rows, need tokens_per_frame - prefix = " + std::to_string(tpf - prefix));
+    if (!aligned16(rope_sin) || !aligned16(rope_cos))
+      return fail(HS_ERR_INVALID, std::string(name) + ": rope tables must be 16-byte aligned");
+  }
+  *qp = QkPrologue{};
+  qp->ln = ln;
+  qp->ln_w = q_norm_w;
+  qp->ln_b = q_norm_b;
+  qp->eps = eps;
+  qp->rope = rope;
+  qp->sin_t = rope_sin;
+  qp->cos_t = rope_cos;
+  qp->prefix = prefix;
+  qp->tokens_per_frame = tpf;
+  *kp = *qp;
+  kp->ln_w = k_norm_w;
+  kp->ln_b = k_norm_b;
+  return HS_OK;
+}
 }  // namespace hs
 
 using namespace hs;
@@ -375,34 +427,24 @@ hs_status hs_attention_fused(hs_ctx* ctx, const void* q, const void* k, const vo
                              const float* rope_sin, const float* rope_cos, uint32_t rope_rows, uint32_t prefix,
                              uint32_t tokens_per_frame) {
   const char* name = "hs_attention_fused";
-  const bool ln = q_norm_w != nullptr;
-  if (ln != (k_norm_w != nullptr) || (ln && (!q_norm_b || !k_norm_b)))
-    return fail(HS_ERR_INVALID, std::string(name) + ": QK-norm needs all of q/k weight and bias, or none");
-  const bool rope = rope_sin != nullptr;
-  if (rope && !rope_cos) return fail(HS_ERR_INVALID, std::string(name) + ": rope_cos missing");
-  const uint32_t tpf = tokens_per_frame ? tokens_per_frame : T;
-  if (rope) {
-    if (prefix > tpf) return fail(HS_ERR_INVALID, std::string(name) + ": prefix > tokens_per_frame");
-    if (static_cast<uint64_t>(rope_rows) < static_cast<uint64_t>(tpf - prefix))
-      return fail(HS_ERR_INVALID, std::string(name) + ": rope tables have " + std::to_string(rope_rows) +
-                                      " rows, need tokens_per_frame - prefix = " + std::to_string(tpf - prefix));
-    if (!aligned16(rope_sin) || !aligned16(rope_cos))
-      return fail(HS_ERR_INVALID, std::string(name) + ": rope tables must be 16-byte aligned");
-  }
-  QkPrologue qp{};
-  qp.ln = ln;
-  qp.ln_w = q_norm_w;
-  qp.ln_b = q_norm_b;
-  qp.eps = eps;
-  qp.rope = rope;
-  qp.sin_t = rope_sin;
-  qp.cos_t = rope_cos;
-  qp.prefix = prefix;
-  qp.tokens_per_frame = tpf;
-  QkPrologue kp = qp;
-  kp.ln_w = k_norm_w;
-  kp.ln_b = k_norm_b;
+  QkPrologue qp, kp;
+  hs_status r = fused_prologues(name, T, q_norm_w, q_norm_b, k_norm_w, k_norm_b, eps, rope_sin, rope_cos, rope_rows,
+                                prefix, tokens_per_frame, &qp, &kp);
+  if (r != HS_OK) return r;
   return attention_impl(ctx, q, k, v, out, S, H, T, D, dtype, scale, qp, kp, name);
+}
+
+hs_status hs_attention_block_fused(hs_ctx* ctx, const void* q, const void* k, const void* v, void* out, uint32_t S,
+                                   uint32_t T, uint32_t H, uint32_t D, hs_dtype dtype, float scale,
+                                   const float* q_norm_w, const float* q_norm_b, const float* k_norm_w,
+                                   const float* k_norm_b, float eps, const float* rope_sin, const float* rope_cos,
+                                   uint32_t rope_rows, uint32_t prefix, uint32_t tokens_per_frame) {
+  const char* name = "hs_attention_block_fused";
+  QkPrologue qp, kp;
+  hs_status r = fused_prologues(name, T, q_norm_w, q_norm_b, k_norm_w, k_norm_b, eps, rope_sin, rope_cos, rope_rows,
+                                prefix, tokens_per_frame, &qp, &kp);
+  if (r != HS_OK) return r;
+  return attention_impl(ctx, q, k, v, out, S, H, T, D, dtype, scale, qp, kp, name, true);
 }
 
 hs_status hs_layernorm(hs_ctx* ctx, const void* x, const float* w, const float* b, void* out, uint64_t rows,

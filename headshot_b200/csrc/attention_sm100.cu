@@ -128,6 +128,8 @@ static_assert(kSmemBytes <= 232448, "shared memory per CTA");
 
 struct Args {
   void* out;
+  RowLayout lo;     // output row layout (head-major, or merged token-major)
+  uint32_t heads;   // sequence index = s * heads + h
   // Max squared norms of the q' and k' rows (f32 bit patterns, set by
   // qk_prep), or null.  Zeroed by the last CTA, ready for the next call,
   // unless shared: then they bound every launch that carries the same
@@ -148,7 +150,7 @@ struct Args {
 };
 
 struct Item {
-  uint32_t seq;
+  uint32_t seq;   // s * heads + h
   uint32_t row0;  // first query row of the item
 };
 
@@ -288,7 +290,8 @@ __device__ void softmax_role(const Args& a, Ctrl* ctl, uint32_t tmem, int warp, 
     if (tile0 >= a.t_q) continue;  // this warpgroup has no rows in the item
     const uint32_t token = tile0 + row;
     const bool valid = token < a.t_q;
-    const uint64_t row_index = static_cast<uint64_t>(it.seq) * a.t_q + token;
+    const uint64_t row_index = static_cast<uint64_t>(it.seq) * a.t_q + token;  // head-major (state arrays)
+    const uint64_t out_index = a.lo.at(it.seq / a.heads, it.seq % a.heads, token);
 
     float m_run = kFixed ? m_fixed : -INFINITY, l = 0.f;
     bool have_o = false;
@@ -428,13 +431,13 @@ __device__ void softmax_role(const Args& a, Ctrl* ctl, uint32_t tmem, int warp, 
       } else {
         const float inv_l = 1.0f / l;
         if (a.out_f32) {
-          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + row_index * kD + 32 * h);
+          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + out_index + 32 * h);
 #pragma unroll
           for (int i = 0; i < 8; ++i)
             dst[i] = make_float4(u2f(o[4 * i]) * inv_l, u2f(o[4 * i + 1]) * inv_l, u2f(o[4 * i + 2]) * inv_l,
                                  u2f(o[4 * i + 3]) * inv_l);
         } else {
-          uint4* dst = reinterpret_cast<uint4*>(static_cast<E*>(a.out) + row_index * kD + 32 * h);
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<E*>(a.out) + out_index + 32 * h);
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             uint4 v;
@@ -510,10 +513,11 @@ __device__ void producer_role(const Args& a, const CUtensorMap* tm_q, const CUte
         continue;
       }
       mbar_arrive_expect_tx(&ctl->q_full[wg][qb], kQTileBytes);
-      tma_load_3d(tm_q, &ctl->q_full[wg][qb], sQ + (wg * kQBufs + qb) * kQTileBytes, 0, static_cast<int>(tile0),
-                  static_cast<int>(it.seq));
+      tma_load_4d(tm_q, &ctl->q_full[wg][qb], sQ + (wg * kQBufs + qb) * kQTileBytes, 0, static_cast<int>(tile0),
+                  static_cast<int>(it.seq % a.heads), static_cast<int>(it.seq / a.heads));
       q_issued[wg] = qi + 1;
     }
+    const int hh = static_cast<int>(it.seq % a.heads), ss = static_cast<int>(it.seq / a.heads);
     for (uint32_t j = 0; ok && j < a.n_kv; ++j, ++g) {
       const uint32_t st = g % kStages;
       if (g >= kStages &&
@@ -523,10 +527,8 @@ __device__ void producer_role(const Args& a, const CUtensorMap* tm_q, const CUte
         break;
       }
       mbar_arrive_expect_tx(&ctl->kv_full[st], 2 * kKvTileBytes);
-      tma_load_3d(tm_k, &ctl->kv_full[st], sK + st * kKvTileBytes, 0, static_cast<int>(j * kBN),
-                  static_cast<int>(it.seq));
-      tma_load_3d(tm_v, &ctl->kv_full[st], sV + st * kKvTileBytes, 0, static_cast<int>(j * kBN),
-                  static_cast<int>(it.seq));
+      tma_load_4d(tm_k, &ctl->kv_full[st], sK + st * kKvTileBytes, 0, static_cast<int>(j * kBN), hh, ss);
+      tma_load_4d(tm_v, &ctl->kv_full[st], sV + st * kKvTileBytes, 0, static_cast<int>(j * kBN), hh, ss);
     }
   }
   // Let every load this thread issued land before the CTA can exit (on the
@@ -759,20 +761,23 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// (SH, T, 64) 16-bit tensor as a 3-D map with box_rows x 64 boxes, 128B
-// swizzle.  Rows past T inside a sequence read as zeros (out-of-bounds fill).
-bool make_map(CUtensorMap* map, const void* base, bool bf16, uint32_t t, uint32_t sh, uint32_t box_rows,
-              std::string* err) {
+// (S, H, T, 64) 16-bit tensor in row layout `l` as a 4-D map (64, T, H, S)
+// with box_rows x 64 boxes, 128B swizzle.  Rows past T inside a sequence read
+// as zeros (out-of-bounds fill).
+bool make_map(CUtensorMap* map, const void* base, const RowLayout& l, bool bf16, uint32_t t, uint32_t heads,
+              uint32_t seqs, uint32_t box_rows, std::string* err) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) {
     if (err) *err = "cuTensorMapEncodeTiled unavailable";
     return false;
   }
-  cuuint64_t dims[3] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(t), static_cast<cuuint64_t>(sh)};
-  cuuint64_t strides[2] = {static_cast<cuuint64_t>(kD) * 2, static_cast<cuuint64_t>(t) * kD * 2};
-  cuuint32_t box[3] = {static_cast<cuuint32_t>(kD), box_rows, 1};
-  cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(t), static_cast<cuuint64_t>(heads),
+                        static_cast<cuuint64_t>(seqs)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(l.t) * 2, static_cast<cuuint64_t>(l.h) * 2,
+                           static_cast<cuuint64_t>(l.s) * 2};
+  cuuint32_t box[4] = {static_cast<cuuint32_t>(kD), box_rows, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
@@ -812,19 +817,21 @@ cudaError_t launch_typed(cudaStream_t stream, const CUtensorMap& mq, const CUten
 
 }  // namespace
 
-cudaError_t launch_attention_sm100(cudaStream_t stream, int elem, const void* q, const void* k, const void* v,
-                                   void* out, int out_code, uint32_t sh, uint32_t t_q, uint32_t t_kv, float scale,
-                                   const AttnState& st, uint32_t max_ctas, int* status, uint32_t* sched,
-                                   unsigned int* qk_norm2, bool norm2_shared, uint64_t timeout_ns,
-                                   std::string* err) {
+cudaError_t launch_attention_sm100(cudaStream_t stream, int elem, const AttnIO& io, uint32_t S, uint32_t H,
+                                   uint32_t t_q, uint32_t t_kv, float scale, const AttnState& st, uint32_t max_ctas,
+                                   int* status, uint32_t* sched, unsigned int* qk_norm2, bool norm2_shared,
+                                   uint64_t timeout_ns, std::string* err) {
+  const uint32_t sh = S * H;
   if (t_q == 0 || sh == 0) return cudaSuccess;
   const bool bf16 = elem == kBF16;
   CUtensorMap mq, mk, mv;
-  if (!make_map(&mq, q, bf16, t_q, sh, kBM, err) || !make_map(&mk, k, bf16, t_kv, sh, kBN, err) ||
-      !make_map(&mv, v, bf16, t_kv, sh, kBN, err))
+  if (!make_map(&mq, io.q, io.lq, bf16, t_q, H, S, kBM, err) || !make_map(&mk, io.k, io.lk, bf16, t_kv, H, S, kBN, err) ||
+      !make_map(&mv, io.v, io.lv, bf16, t_kv, H, S, kBN, err))
     return cudaErrorInvalidValue;
   Args a{};
-  a.out = out;
+  a.out = io.out;
+  a.lo = io.lo;
+  a.heads = H;
   a.t_q = t_q;
   a.t_kv = t_kv;
   a.n_kv = (t_kv + kBN - 1) / kBN;
@@ -835,7 +842,7 @@ cudaError_t launch_attention_sm100(cudaStream_t stream, int elem, const void* q,
     return cudaErrorInvalidValue;
   }
   a.n_items = static_cast<uint32_t>(items);
-  a.out_f32 = out_code == kF32;
+  a.out_f32 = io.out_code == kF32;
   a.scale_log2 = scale * 1.4426950408889634f;
   a.st = st;
   a.status = status;

@@ -42,6 +42,36 @@ struct AttnState {
   int store = 0;       // write the state instead of the normalised output
 };
 
+// Where row (s, h, t) of a (S, H, T, 64) tensor starts, in elements: the
+// strides of t, h and s (the 64 elements of a row are contiguous).
+struct RowLayout {
+  uint64_t t = 64, h = 0, s = 0;
+  // (S, H, T, 64) contiguous, the reference's attention layout (ops.rs:228).
+  static RowLayout head_major(uint32_t H, uint32_t T) {
+    return RowLayout{64, static_cast<uint64_t>(T) * 64, static_cast<uint64_t>(H) * T * 64};
+  }
+  // (S*T, H*64) rows of `row_elems` >= H*64 elements (projection outputs and
+  // the merged attention output, ops.rs:185-200 / 255-267).
+  static RowLayout token_major(uint32_t H, uint32_t T, uint64_t row_elems) {
+    return RowLayout{row_elems, 64, static_cast<uint64_t>(T) * row_elems};
+  }
+  __host__ __device__ uint64_t at(uint64_t s_, uint64_t h_, uint64_t t_) const { return s_ * s + h_ * h + t_ * t; }
+};
+
+// Operands of one attention launch: 16-bit q, k, v rows of type `elem` and
+// the output (kF32 or `elem`), each with its own row layout.
+struct AttnIO {
+  const void* q = nullptr;
+  RowLayout lq;
+  const void* k = nullptr;
+  RowLayout lk;
+  const void* v = nullptr;
+  RowLayout lv;
+  void* out = nullptr;
+  RowLayout lo;
+  int out_code = 0;
+};
+
 // Flash attention on tcgen05 (D = 64), persistent: at most `max_ctas` CTAs
 // (0 = one per SM) take the (sequence, 256-row) work items from the counter
 // pair `sched` (2 x u32, zero before the launch; the kernel leaves it zero,
@@ -53,15 +83,17 @@ struct AttnState {
 // softmax uses a fixed offset instead of a running max.  Zeroed by the
 // kernel unless `norm2_shared`: then the caller guarantees they bound every
 // launch that carries the same state `st` (all ring steps) and resets them.
-cudaError_t launch_attention_sm100(cudaStream_t stream, int elem, const void* q, const void* k, const void* v,
-                                   void* out, int out_code, uint32_t sh, uint32_t t_q, uint32_t t_kv, float scale,
-                                   const AttnState& st, uint32_t max_ctas, int* status, uint32_t* sched,
-                                   unsigned int* qk_norm2, bool norm2_shared, uint64_t timeout_ns,
-                                   std::string* err);
+// S sequences of H heads; the state arrays are indexed head-major.
+cudaError_t launch_attention_sm100(cudaStream_t stream, int elem, const AttnIO& io, uint32_t S, uint32_t H,
+                                   uint32_t t_q, uint32_t t_kv, float scale, const AttnState& st, uint32_t max_ctas,
+                                   int* status, uint32_t* sched, unsigned int* qk_norm2, bool norm2_shared,
+                                   uint64_t timeout_ns, std::string* err);
 
 // Row prep for K (and for casts): out = RoPE(LN(x)) in `out_code` storage.
-cudaError_t launch_qk_prep(cudaStream_t stream, const void* x, int in_code, void* out, int out_code,
-                           uint64_t rows, uint32_t t, const QkPrologue& p);
+// Reads x (S, H, T, 64) in layout `lx`, writes head-major 16-bit or f32
+// rows.
+cudaError_t launch_qk_prep(cudaStream_t stream, const void* x, int in_code, const RowLayout& lx, void* out,
+                           int out_code, uint32_t S, uint32_t H, uint32_t t, const QkPrologue& p);
 
 // Companion ops of the reference engine.
 cudaError_t launch_layernorm(cudaStream_t stream, const void* x, void* out, int code, const float* w,

@@ -154,16 +154,27 @@ extern "C" hs_status hs_attention_fused_noalloc(void* stream, int* status, const
     uint8_t* k_rows = q_rows + kNoAllocRegionBytes;
     qp.norm2_max = p.sched + 2;
     kp.norm2_max = p.sched + 3;
-    e = hs::launch_qk_prep(st, q, code, q_rows, code, rows, T, qp);
-    if (e == cudaSuccess) e = hs::launch_qk_prep(st, k, code, k_rows, code, rows, T, kp);
+    const hs::RowLayout hm = hs::RowLayout::head_major(H, T);
+    e = hs::launch_qk_prep(st, q, code, hm, q_rows, code, S, H, T, qp);
+    if (e == cudaSuccess) e = hs::launch_qk_prep(st, k, code, hm, k_rows, code, S, H, T, kp);
     if (e != cudaSuccess) return hs::abi_cuda_fail(e, name);
     q_use = q_rows;
     k_use = k_rows;
   }
   std::string err;
   hs::AttnState state{};
-  e = hs::launch_attention_sm100(st, code, q_use, k_use, v, out, code, S * H, T, T, scale, state, 0, status_word,
-                                 p.sched, (ln || rope) ? p.sched + 2 : nullptr, false, kNoAllocTimeoutNs, &err);
+  hs::AttnIO io;
+  io.q = q_use;
+  io.lq = hs::RowLayout::head_major(H, T);
+  io.k = k_use;
+  io.lk = io.lq;
+  io.v = v;
+  io.lv = io.lq;
+  io.out = out;
+  io.lo = io.lq;
+  io.out_code = code;
+  e = hs::launch_attention_sm100(st, code, io, S, H, T, T, scale, state, 0, status_word, p.sched,
+                                 (ln || rope) ? p.sched + 2 : nullptr, false, kNoAllocTimeoutNs, &err);
   if (e != cudaSuccess)
     return hs::abi_fail(HS_ERR_CUDA, std::string(name) + ": " + (err.empty() ? cudaGetErrorString(e) : err));
   return HS_OK;

@@ -157,8 +157,8 @@ __device__ __forceinline__ float store_halves(Out* row, int g, const float (&v)[
 // and reused for every sequence.  Each thread issues the loads of all its
 // rows before any arithmetic, so enough bytes are in flight for HBM.
 template <typename In, typename Out>
-__global__ void __launch_bounds__(256) qk_prep_kernel(const In* __restrict__ x, Out* __restrict__ out, uint32_t sh,
-                                                      uint32_t t, QkPrologue p) {
+__global__ void __launch_bounds__(256) qk_prep_kernel(const In* __restrict__ x, RowLayout lx, Out* __restrict__ out,
+                                                      uint32_t sh, uint32_t heads, uint32_t t, QkPrologue p) {
   constexpr int kRows = sizeof(In) == 4 ? kPrepSeqPerBlock / 2 : kPrepSeqPerBlock;  // rows per pass
   const int lt = threadIdx.x >> 3;  // token within the block
   const int g = threadIdx.x & 7;
@@ -166,12 +166,14 @@ __global__ void __launch_bounds__(256) qk_prep_kernel(const In* __restrict__ x, 
   const bool tok_ok = tok < t;
   const uint32_t seq0 = blockIdx.y * kPrepSeqPerBlock;
   const uint32_t seq_end = min(sh, seq0 + kPrepSeqPerBlock);
+  // Input row of sequence q = s*heads + h in its own layout; output rows are head-major.
+  auto in_at = [&](uint32_t q) { return lx.at(q / heads, q % heads, tok); };
   auto row_at = [&](uint32_t q) { return (static_cast<uint64_t>(q) * t + tok) * 64; };
 
   RawHalves<In> raw[kRows];
 #pragma unroll
   for (int u = 0; u < kRows; ++u) {
-    if (tok_ok && seq0 + u < seq_end) raw[u].load(x + row_at(seq0 + u), g);
+    if (tok_ok && seq0 + u < seq_end) raw[u].load(x + in_at(seq0 + u), g);
     else raw[u].zero();
   }
   // This thread's table columns (pass-through rows: sin 0, cos 1).  Scalar
@@ -208,7 +210,7 @@ __global__ void __launch_bounds__(256) qk_prep_kernel(const In* __restrict__ x, 
     if (q0 != seq0) {  // f32 storage: a second pass over the block's sequences
 #pragma unroll
       for (int u = 0; u < kRows; ++u) {
-        if (tok_ok && q0 + u < seq_end) raw[u].load(x + row_at(q0 + u), g);
+        if (tok_ok && q0 + u < seq_end) raw[u].load(x + in_at(q0 + u), g);
         else raw[u].zero();
       }
     }
@@ -344,19 +346,19 @@ inline unsigned blocks_for(uint64_t threads, unsigned per_block) {
 }
 
 template <typename In>
-cudaError_t prep_dispatch_out(cudaStream_t stream, const In* x, void* out, int out_code, uint64_t rows, uint32_t t,
-                              const QkPrologue& p) {
-  const uint32_t sh = static_cast<uint32_t>(rows / t);
+cudaError_t prep_dispatch_out(cudaStream_t stream, const In* x, const RowLayout& lx, void* out, int out_code,
+                              uint32_t sh, uint32_t heads, uint32_t t, const QkPrologue& p) {
   const dim3 grid((t + kPrepTokens - 1) / kPrepTokens, (sh + kPrepSeqPerBlock - 1) / kPrepSeqPerBlock, 1);
   switch (out_code) {
     case kBF16:
-      qk_prep_kernel<In, __nv_bfloat16><<<grid, 256, 0, stream>>>(x, static_cast<__nv_bfloat16*>(out), sh, t, p);
+      qk_prep_kernel<In, __nv_bfloat16><<<grid, 256, 0, stream>>>(x, lx, static_cast<__nv_bfloat16*>(out), sh, heads,
+                                                                   t, p);
       break;
     case kF16:
-      qk_prep_kernel<In, __half><<<grid, 256, 0, stream>>>(x, static_cast<__half*>(out), sh, t, p);
+      qk_prep_kernel<In, __half><<<grid, 256, 0, stream>>>(x, lx, static_cast<__half*>(out), sh, heads, t, p);
       break;
     default:
-      qk_prep_kernel<In, float><<<grid, 256, 0, stream>>>(x, static_cast<float*>(out), sh, t, p);
+      qk_prep_kernel<In, float><<<grid, 256, 0, stream>>>(x, lx, static_cast<float*>(out), sh, heads, t, p);
       break;
   }
   return cudaGetLastError();
@@ -411,13 +413,15 @@ struct PermuteRun {
 
 }  // namespace
 
-cudaError_t launch_qk_prep(cudaStream_t stream, const void* x, int in_code, void* out, int out_code, uint64_t rows,
-                           uint32_t t, const QkPrologue& p) {
-  if (rows == 0) return cudaSuccess;
+cudaError_t launch_qk_prep(cudaStream_t stream, const void* x, int in_code, const RowLayout& lx, void* out,
+                           int out_code, uint32_t S, uint32_t H, uint32_t t, const QkPrologue& p) {
+  const uint32_t sh = S * H;
+  if (sh == 0 || t == 0) return cudaSuccess;
   switch (in_code) {
-    case kBF16: return prep_dispatch_out(stream, static_cast<const __nv_bfloat16*>(x), out, out_code, rows, t, p);
-    case kF16: return prep_dispatch_out(stream, static_cast<const __half*>(x), out, out_code, rows, t, p);
-    default: return prep_dispatch_out(stream, static_cast<const float*>(x), out, out_code, rows, t, p);
+    case kBF16:
+      return prep_dispatch_out(stream, static_cast<const __nv_bfloat16*>(x), lx, out, out_code, sh, H, t, p);
+    case kF16: return prep_dispatch_out(stream, static_cast<const __half*>(x), lx, out, out_code, sh, H, t, p);
+    default: return prep_dispatch_out(stream, static_cast<const float*>(x), lx, out, out_code, sh, H, t, p);
   }
 }
 

@@ -309,7 +309,7 @@ hs_status hs_ring_attention_fused(hs_ring* ring, const void* q, const void* k, c
   }
   {
     hs::ProfScope prof(ctx, st, "qk_prep");
-    e = bounded ? hs::launch_qk_prep(st, k, code, b0, code, rows, tr, kp)
+    e = bounded ? hs::launch_qk_prep(st, k, code, hs::RowLayout::head_major(H, tr), b0, code, 1, H, tr, kp)
                 : cudaMemcpyAsync(b0, k, rows * row_bytes, cudaMemcpyDeviceToDevice, st);
   }
   if (e != cudaSuccess) return hs::abi_cuda_fail(e, "ring K' prep");
@@ -318,7 +318,7 @@ hs_status hs_ring_attention_fused(hs_ring* ring, const void* q, const void* k, c
   if (bounded) {
     {
       hs::ProfScope prof(ctx, st, "qk_prep");
-      e = hs::launch_qk_prep(st, q, code, ring->state, code, rows, tr, qp);
+      e = hs::launch_qk_prep(st, q, code, hs::RowLayout::head_major(H, tr), ring->state, code, 1, H, tr, qp);
     }
     if (e != cudaSuccess) return hs::abi_cuda_fail(e, "ring Q' prep");
     q_use = ring->state;
@@ -364,8 +364,17 @@ hs_status hs_ring_attention_fused(hs_ring* ring, const void* q, const void* k, c
     std::string err;
     {
       hs::ProfScope prof(ctx, st, "attention");
-      e = hs::launch_attention_sm100(st, code, q_use, cur, cur + static_cast<size_t>(H) * src_len * row_bytes, out,
-                                     code, H, tr, src_len, scale, state, 0, ctx->d_status, ctx->d_sched,
+      hs::AttnIO io;
+      io.q = q_use;
+      io.lq = hs::RowLayout::head_major(H, tr);
+      io.k = cur;
+      io.lk = hs::RowLayout::head_major(H, src_len);
+      io.v = cur + static_cast<size_t>(H) * src_len * row_bytes;
+      io.lv = io.lk;
+      io.out = out;
+      io.lo = io.lq;
+      io.out_code = code;
+      e = hs::launch_attention_sm100(st, code, io, 1, H, tr, src_len, scale, state, 0, ctx->d_status, ctx->d_sched,
                                      bounded ? ring->norm2 : nullptr, true, hs::ctx_timeout_ns(ctx), &err);
     }
     if (e != cudaSuccess)

@@ -111,19 +111,7 @@ class GpuContext:
                                    0.0 if scale is None else float(scale)))
         return out
 
-    def attention_fused(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, qk_norm: QkNorm | None = None,
-                        rope: Rope | None = None, scale: float | None = None,
-                        out: torch.Tensor | None = None) -> torch.Tensor:
-        """QK-norm -> RoPE -> attention (block.rs:136-148) in one call."""
-        assert q.dim() == 4, "attention wants (S,H,T,D)"
-        assert q.shape == k.shape and q.shape == v.shape, "q/k/v shape mismatch"
-        assert q.dtype == k.dtype == v.dtype, "q/k/v dtype mismatch"
-        s, h, t, d = q.shape
-        for n, x in (("q", q), ("k", k), ("v", v)):
-            self._check_tensor(x, n)
-        if out is None:
-            out = torch.empty_like(q)
-        assert out.shape == q.shape and out.dtype == q.dtype
+    def _prologue_args(self, d: int, t: int, qk_norm: QkNorm | None, rope: Rope | None) -> tuple:
         n_args = [None] * 4
         eps = 1e-5
         if qk_norm is not None:
@@ -143,11 +131,49 @@ class GpuContext:
             rows = rope.sin.numel() // d
             prefix = rope.prefix
             tpf = rope.tokens_per_frame or t
+        return (*[_ptr(x) for x in n_args], float(eps), _ptr(r_sin), _ptr(r_cos), rows, prefix, tpf)
+
+    def attention_fused(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, qk_norm: QkNorm | None = None,
+                        rope: Rope | None = None, scale: float | None = None,
+                        out: torch.Tensor | None = None) -> torch.Tensor:
+        """QK-norm -> RoPE -> attention (block.rs:136-148) in one call."""
+        assert q.dim() == 4, "attention wants (S,H,T,D)"
+        assert q.shape == k.shape and q.shape == v.shape, "q/k/v shape mismatch"
+        assert q.dtype == k.dtype == v.dtype, "q/k/v dtype mismatch"
+        s, h, t, d = q.shape
+        for n, x in (("q", q), ("k", k), ("v", v)):
+            self._check_tensor(x, n)
+        if out is None:
+            out = torch.empty_like(q)
+        assert out.shape == q.shape and out.dtype == q.dtype
+        pro = self._prologue_args(d, t, qk_norm, rope)
         self._bind_stream()
         check(self._L.hs_attention_fused(
             self._h, _ptr(q), _ptr(k), _ptr(v), _ptr(out), s, h, t, d, _code(q),
-            0.0 if scale is None else float(scale), *[_ptr(x) for x in n_args], float(eps), _ptr(r_sin), _ptr(r_cos),
-            rows, prefix, tpf))
+            0.0 if scale is None else float(scale), *pro))
+        return out
+
+    def attention_block(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, s: int, t: int, heads: int,
+                        qk_norm: QkNorm | None = None, rope: Rope | None = None, scale: float | None = None,
+                        out: torch.Tensor | None = None) -> torch.Tensor:
+        """Block::forward's attention section (block.rs:130-149) on the projection layout:
+        q, k, v are the (S*T, H*D) outputs of the q/k/v linears; returns the (S*T, H*D)
+        merged attention output (what attn_merge hands to the proj linear)."""
+        assert q.shape == k.shape and q.shape == v.shape, "q/k/v shape mismatch"
+        assert q.dtype == k.dtype == v.dtype, "q/k/v dtype mismatch"
+        assert q.numel() % (s * t * heads) == 0, "shape"
+        d = q.numel() // (s * t * heads)
+        assert q.shape[-1] == heads * d and q.numel() == s * t * heads * d, "q must be (S*T, H*D)"
+        for n, x in (("q", q), ("k", k), ("v", v)):
+            self._check_tensor(x, n)
+        if out is None:
+            out = torch.empty_like(q)
+        assert out.shape == q.shape and out.dtype == q.dtype
+        pro = self._prologue_args(d, t, qk_norm, rope)
+        self._bind_stream()
+        check(self._L.hs_attention_block_fused(
+            self._h, _ptr(q), _ptr(k), _ptr(v), _ptr(out), s, t, heads, d, _code(q),
+            0.0 if scale is None else float(scale), *pro))
         return out
 
     def layernorm(self, x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:

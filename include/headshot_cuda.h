@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define HS_ABI_VERSION 1u
+#define HS_ABI_VERSION 2u
 
 #if defined(__GNUC__)
 #define HS_API __attribute__((visibility("default")))
@@ -116,8 +116,8 @@ HS_API hs_status hs_attention(hs_ctx* ctx, const void* q, const void* k, const v
 /* The attention section of Block::forward (src/model/block.rs:136-148) as
  * one op: QK-norm (LayerNorm over D with f32 weight/bias, eps) on q and k,
  * then 2D RoPE (rotate-half, src/engine/rope.rs:48-55) on q and k, then
- * attention.  The Q side runs inside the attention kernel's load prologue;
- * K is normalised/rotated once into context scratch.
+ * attention.  Q and K are normalised/rotated once into context scratch
+ * (one pass each), which also bounds every score for the softmax.
  *   q_norm_w == NULL: no QK-norm (k_norm_w must then be NULL too).
  *   rope_sin == NULL: no RoPE.  Otherwise the table row of token t is
  *   (t mod tokens_per_frame) - prefix and tokens with (t mod tokens_per_frame)
@@ -128,6 +128,22 @@ HS_API hs_status hs_attention_fused(hs_ctx* ctx, const void* q, const void* k, c
                              const float* q_norm_b, const float* k_norm_w, const float* k_norm_b, float eps,
                              const float* rope_sin, const float* rope_cos, uint32_t rope_rows, uint32_t prefix,
                              uint32_t tokens_per_frame);
+
+/* Block::forward's whole attention section (src/model/block.rs:130-149) in
+ * the layout the projections produce and consume: q, k, v are the three
+ * (S*T, H*D) outputs of the q/k/v linears (token-major, the input of
+ * split_heads, ops.rs:185-200) and out is (S*T, H*D), the output of
+ * attn_merge (ops.rs:255-267) that the proj linear reads.  Same arguments
+ * and results as hs_attention_fused otherwise; the split, QK-norm, RoPE,
+ * attention and merge run as one prep pass per q/k and one attention
+ * kernel reading v and writing out in place (no head-major copies of v or
+ * out).  Note the argument order S, T, H, D of split_heads. */
+HS_API hs_status hs_attention_block_fused(hs_ctx* ctx, const void* q, const void* k, const void* v, void* out,
+                                          uint32_t S, uint32_t T, uint32_t H, uint32_t D, hs_dtype dtype,
+                                          float scale, const float* q_norm_w, const float* q_norm_b,
+                                          const float* k_norm_w, const float* k_norm_b, float eps,
+                                          const float* rope_sin, const float* rope_cos, uint32_t rope_rows,
+                                          uint32_t prefix, uint32_t tokens_per_frame);
 
 /* No counterpart in the reference.  hs_attention_fused for callers that
  * cannot let the library allocate device memory: hosts whose device memory

@@ -39,7 +39,7 @@ def test_python_bindings_cover_the_header(L):
 
 
 def test_abi_version(L):
-    assert L.hs_abi_version() == 1
+    assert L.hs_abi_version() == 2
 
 
 def test_rope_host_helpers_match_oracle(L):

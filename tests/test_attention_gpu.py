@@ -226,3 +226,79 @@ def test_split_merge_roundtrip(gpu_ctx, dtype):
         merged = gpu_ctx.attn_merge(heads)
         gpu_ctx.sync()
         np.testing.assert_array_equal(host(merged), x)
+
+
+# ---- the block's attention section on the projection layout (f1) ------------
+
+def _block_inputs(s, h, t, dtype, seed):
+    d = 64
+    rng = np.random.default_rng(seed)
+    # the three (S*T, H*D) projection outputs Block::forward feeds split_heads
+    qt, kt, vt = (rounded(rng.standard_normal((s * t, h * d), np.float32), dtype) for _ in range(3))
+    qw, kw = (rng.uniform(0.5, 1.5, d).astype(np.float32) for _ in range(2))
+    qb, kb = (rng.uniform(-0.2, 0.2, d).astype(np.float32) for _ in range(2))
+    return qt, kt, vt, (qw, qb, kw, kb)
+
+
+@pytest.mark.parametrize("dtype,s,t,tpf", [("bf16", 2, 1374, 1374), ("f16", 3, 1374, 1374), ("bf16", 1, 2748, 1374)])
+def test_block_fused_matches_oracle(gpu_ctx, dtype, s, t, tpf):
+    # split_heads -> QK-norm -> RoPE -> attention -> attn_merge (block.rs:130-149)
+    # in one call on the token-major layout, against the oracle's five steps.
+    h, d, prefix, eps = 4, 64, 5, 1e-6
+    qt, kt, vt, (qw, qb, kw, kb) = _block_inputs(s, h, t, dtype, 31 + t)
+    sin, cos = oracle.rope_tables(37, 37)
+    q, k, v = (oracle.split_heads(x, s, t, h, d) for x in (qt, kt, vt))
+    qn = rounded(oracle.qk_prep(q, qw, qb, eps, sin, cos, prefix, tpf), dtype)
+    kn = rounded(oracle.qk_prep(k, kw, kb, eps, sin, cos, prefix, tpf), dtype)
+    ref = oracle.attn_merge(oracle.attention(qn, kn, v))
+    c = lambda a: torch.from_numpy(a).cuda()  # noqa: E731
+    out = gpu_ctx.attention_block(dev(qt, dtype), dev(kt, dtype), dev(vt, dtype), s, t, h,
+                                  qk_norm=QkNorm(c(qw), c(qb), c(kw), c(kb), eps),
+                                  rope=Rope(c(sin), c(cos), prefix, tpf))
+    gpu_ctx.sync()
+    assert out.shape == (s * t, h * d)
+    gate(host(out), ref)
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+def test_block_plain_reads_token_major_directly(gpu_ctx, dtype):
+    # No QK-norm/RoPE: the kernel's tensor maps read q, k, v straight from the
+    # token-major rows (no prep pass) and the epilogue writes merged rows.
+    s, h, t, d = 2, 3, 777, 64
+    qt, kt, vt, _ = _block_inputs(s, h, t, dtype, 5)
+    q, k, v = (oracle.split_heads(x, s, t, h, d) for x in (qt, kt, vt))
+    ref = oracle.attn_merge(oracle.attention(q, k, v))
+    out = gpu_ctx.attention_block(dev(qt, dtype), dev(kt, dtype), dev(vt, dtype), s, t, h)
+    gpu_ctx.sync()
+    gate(host(out), ref)
+
+
+def test_block_fused_equals_split_fused_merge_on_gpu(gpu_ctx):
+    # Same kernel, two layouts: the block entry point must reproduce
+    # split_heads + attention_fused + attn_merge bit for bit.
+    s, h, t, d, prefix, eps = 2, 4, 1374, 64, 5, 1e-6
+    qt, kt, vt, (qw, qb, kw, kb) = _block_inputs(s, h, t, "bf16", 77)
+    sin, cos = oracle.rope_tables(37, 37)
+    c = lambda a: torch.from_numpy(a).cuda()  # noqa: E731
+    norm, rope = QkNorm(c(qw), c(qb), c(kw), c(kb), eps), Rope(c(sin), c(cos), prefix, t)
+    qd, kd, vd = (dev(x, "bf16") for x in (qt, kt, vt))
+    merged = gpu_ctx.attention_block(qd, kd, vd, s, t, h, qk_norm=norm, rope=rope)
+    heads = [gpu_ctx.split_heads(x, s, t, h, d) for x in (qd, kd, vd)]
+    two_step = gpu_ctx.attn_merge(gpu_ctx.attention_fused(*heads, qk_norm=norm, rope=rope))
+    gpu_ctx.sync()
+    assert torch.equal(merged, two_step.reshape(merged.shape))
+
+
+def test_block_fused_f32_storage(gpu_ctx):
+    s, h, t, d, prefix, eps = 1, 2, 500, 64, 5, 1e-6
+    qt, kt, vt, (qw, qb, kw, kb) = _block_inputs(s, h, t, "f32", 8)
+    sin, cos = oracle.rope_tables(37, 37)
+    q, k, v = (oracle.split_heads(x, s, t, h, d) for x in (qt, kt, vt))
+    ref = oracle.attn_merge(oracle.attention(oracle.qk_prep(q, qw, qb, eps, sin, cos, prefix, t),
+                                             oracle.qk_prep(k, kw, kb, eps, sin, cos, prefix, t), v))
+    c = lambda a: torch.from_numpy(a).cuda()  # noqa: E731
+    out = gpu_ctx.attention_block(dev(qt, "f32"), dev(kt, "f32"), dev(vt, "f32"), s, t, h,
+                                  qk_norm=QkNorm(c(qw), c(qb), c(kw), c(kb), eps), rope=Rope(c(sin), c(cos), prefix, t))
+    gpu_ctx.sync()
+    assert out.dtype == torch.float32
+    gate(host(out), ref)
