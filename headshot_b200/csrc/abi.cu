@@ -145,19 +145,24 @@ hs_status attention_impl(hs_ctx* ctx, const void* q, const void* k, const void* 
   kpn.norm2_max = norm2 ? norm2 + 1 : nullptr;
   const QkPrologue none{};
   const QkPrologue* pro[3] = {&qpn, &kpn, &none};
-  static const char* const what[3] = {"qk_prep(q)", "qk_prep(k)", "cast(v)"};
+  // Every tensor that needs a pass goes through one qk_prep launch.
+  PrepJob jobs[3];
+  int n_jobs = 0;
   uint8_t* cursor = static_cast<uint8_t*>(scratch);
-  cudaError_t e;
   for (int i = 0; i < 3; ++i) {
     if (direct[i]) continue;
-    {
-      ProfScope prof(ctx, st, "qk_prep");
-      e = launch_qk_prep(st, use[i], code, given, cursor, elem, S, H, T, *pro[i]);
-    }
-    if (e != cudaSuccess) return cuda_fail(e, what[i]);
+    jobs[n_jobs++] = PrepJob{use[i], given, cursor, *pro[i]};
     use[i] = cursor;
     lay[i] = head_major;
     cursor += tile_bytes;
+  }
+  cudaError_t e = cudaSuccess;
+  if (n_jobs) {
+    {
+      ProfScope prof(ctx, st, "qk_prep");
+      e = launch_qk_prep(st, code, elem, S, H, T, jobs, n_jobs);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "qk_prep");
   }
   std::string err;
   AttnState state{};

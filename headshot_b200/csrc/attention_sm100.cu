@@ -101,10 +101,12 @@ enum : int {
 
 // Barrier phases are counted per barrier across all items of a CTA; every
 // waiter knows how many completions precede the one it wants.  Parity waits
-// cannot tell phase n from phase n+2, so each barrier is arranged such that
-// its next completion needs an action of the waiter taken after the wait:
-// S buffers are doubled by tile parity, PV-only batches at the end of an
-// item complete pv_done instead of an S buffer, Q buffers are doubled.
+// cannot tell phase n from phase n+2 (nor n from n-2), so each barrier is
+// arranged such that its next completion needs an action of the waiter
+// taken after the wait, and every waiter waits the completions it needs in
+// order (never one two ahead of the last it saw): S buffers are doubled by
+// tile parity, PV-only batches at the end of an item complete pv_done
+// instead of an S buffer (the epilogue waits both), Q buffers are doubled.
 struct Ctrl {
   uint64_t kv_full[kStages];      // K and V tile of a stage landed (one transaction count)
   uint64_t kv_empty[kStages];     // both MMA warps are done with the stage
@@ -409,7 +411,13 @@ __device__ void softmax_role(const Args& a, Ctrl* ctl, uint32_t tmem, int warp, 
       if (lane == 0) mbar_arrive(&ctl->p_full[wg][b]);
     }
 
-    // PV(n-1) is the item's last PV-only batch.
+    // PV(n-1) is the item's last PV-only batch.  Wait for the item's
+    // pv_done completions in order: a warp that runs ahead of its
+    // warpgroup can get here before PV(n-2) has even been issued, and a
+    // parity wait for a completion two phases ahead would pass at once.
+    if (pv_last && !warp_wait(&ctl->pv_done[wg], (base_bits >> 2) & 1, abort_flag, a.status, kSiteODone,
+                              a.timeout_ns))
+      return;
     if (!warp_wait(&ctl->pv_done[wg], ((base_bits >> 2) + pv_last) & 1, abort_flag, a.status, kSiteODone,
                    a.timeout_ns))
       return;

@@ -90,6 +90,22 @@ cudaError_t launch_attention_sm100(cudaStream_t stream, int elem, const AttnIO& 
                                    uint64_t timeout_ns, std::string* err);
 
 // Row prep for K (and for casts): out = RoPE(LN(x)) in `out_code` storage.
+// One tensor of a qk_prep launch: x (S, H, T, 64) in layout `lx` in, head-
+// major rows out, with its own prologue.
+struct PrepJob {
+  const void* x = nullptr;
+  RowLayout lx;
+  void* out = nullptr;
+  QkPrologue p;
+};
+constexpr int kMaxPrepJobs = 3;
+struct PrepJobs {
+  PrepJob job[kMaxPrepJobs];
+};
+// Up to kMaxPrepJobs tensors of the same shape and types in one launch.
+cudaError_t launch_qk_prep(cudaStream_t stream, int in_code, int out_code, uint32_t S, uint32_t H, uint32_t t,
+                           const PrepJob* jobs, int n_jobs);
+
 // Reads x (S, H, T, 64) in layout `lx`, writes head-major 16-bit or f32
 // rows.
 cudaError_t launch_qk_prep(cudaStream_t stream, const void* x, int in_code, const RowLayout& lx, void* out,

@@ -155,8 +155,8 @@ extern "C" hs_status hs_attention_fused_noalloc(void* stream, int* status, const
     qp.norm2_max = p.sched + 2;
     kp.norm2_max = p.sched + 3;
     const hs::RowLayout hm = hs::RowLayout::head_major(H, T);
-    e = hs::launch_qk_prep(st, q, code, hm, q_rows, code, S, H, T, qp);
-    if (e == cudaSuccess) e = hs::launch_qk_prep(st, k, code, hm, k_rows, code, S, H, T, kp);
+    const hs::PrepJob jobs[2] = {{q, hm, q_rows, qp}, {k, hm, k_rows, kp}};
+    e = hs::launch_qk_prep(st, code, code, S, H, T, jobs, 2);
     if (e != cudaSuccess) return hs::abi_cuda_fail(e, name);
     q_use = q_rows;
     k_use = k_rows;

@@ -157,8 +157,13 @@ __device__ __forceinline__ float store_halves(Out* row, int g, const float (&v)[
 // and reused for every sequence.  Each thread issues the loads of all its
 // rows before any arithmetic, so enough bytes are in flight for HBM.
 template <typename In, typename Out>
-__global__ void __launch_bounds__(256) qk_prep_kernel(const In* __restrict__ x, RowLayout lx, Out* __restrict__ out,
-                                                      uint32_t sh, uint32_t heads, uint32_t t, QkPrologue p) {
+__global__ void __launch_bounds__(256) qk_prep_kernel(PrepJobs jobs, uint32_t sh, uint32_t heads, uint32_t t) {
+  // blockIdx.z picks the tensor (q, k, v casts) of this launch.
+  const PrepJob& job = jobs.job[blockIdx.z];
+  const In* __restrict__ x = static_cast<const In*>(job.x);
+  Out* __restrict__ out = static_cast<Out*>(job.out);
+  const RowLayout lx = job.lx;
+  const QkPrologue& p = job.p;
   constexpr int kRows = sizeof(In) == 4 ? kPrepSeqPerBlock / 2 : kPrepSeqPerBlock;  // rows per pass
   const int lt = threadIdx.x >> 3;  // token within the block
   const int g = threadIdx.x & 7;
@@ -346,20 +351,13 @@ inline unsigned blocks_for(uint64_t threads, unsigned per_block) {
 }
 
 template <typename In>
-cudaError_t prep_dispatch_out(cudaStream_t stream, const In* x, const RowLayout& lx, void* out, int out_code,
-                              uint32_t sh, uint32_t heads, uint32_t t, const QkPrologue& p) {
-  const dim3 grid((t + kPrepTokens - 1) / kPrepTokens, (sh + kPrepSeqPerBlock - 1) / kPrepSeqPerBlock, 1);
+cudaError_t prep_dispatch_out(cudaStream_t stream, const PrepJobs& jobs, int n_jobs, int out_code, uint32_t sh,
+                              uint32_t heads, uint32_t t) {
+  const dim3 grid((t + kPrepTokens - 1) / kPrepTokens, (sh + kPrepSeqPerBlock - 1) / kPrepSeqPerBlock, n_jobs);
   switch (out_code) {
-    case kBF16:
-      qk_prep_kernel<In, __nv_bfloat16><<<grid, 256, 0, stream>>>(x, lx, static_cast<__nv_bfloat16*>(out), sh, heads,
-                                                                   t, p);
-      break;
-    case kF16:
-      qk_prep_kernel<In, __half><<<grid, 256, 0, stream>>>(x, lx, static_cast<__half*>(out), sh, heads, t, p);
-      break;
-    default:
-      qk_prep_kernel<In, float><<<grid, 256, 0, stream>>>(x, lx, static_cast<float*>(out), sh, heads, t, p);
-      break;
+    case kBF16: qk_prep_kernel<In, __nv_bfloat16><<<grid, 256, 0, stream>>>(jobs, sh, heads, t); break;
+    case kF16: qk_prep_kernel<In, __half><<<grid, 256, 0, stream>>>(jobs, sh, heads, t); break;
+    default: qk_prep_kernel<In, float><<<grid, 256, 0, stream>>>(jobs, sh, heads, t); break;
   }
   return cudaGetLastError();
 }
@@ -413,16 +411,24 @@ struct PermuteRun {
 
 }  // namespace
 
+cudaError_t launch_qk_prep(cudaStream_t stream, int in_code, int out_code, uint32_t S, uint32_t H, uint32_t t,
+                           const PrepJob* jobs, int n_jobs) {
+  const uint32_t sh = S * H;
+  if (sh == 0 || t == 0 || n_jobs == 0) return cudaSuccess;
+  if (n_jobs < 0 || n_jobs > kMaxPrepJobs) return cudaErrorInvalidValue;
+  PrepJobs all{};
+  for (int i = 0; i < n_jobs; ++i) all.job[i] = jobs[i];
+  switch (in_code) {
+    case kBF16: return prep_dispatch_out<__nv_bfloat16>(stream, all, n_jobs, out_code, sh, H, t);
+    case kF16: return prep_dispatch_out<__half>(stream, all, n_jobs, out_code, sh, H, t);
+    default: return prep_dispatch_out<float>(stream, all, n_jobs, out_code, sh, H, t);
+  }
+}
+
 cudaError_t launch_qk_prep(cudaStream_t stream, const void* x, int in_code, const RowLayout& lx, void* out,
                            int out_code, uint32_t S, uint32_t H, uint32_t t, const QkPrologue& p) {
-  const uint32_t sh = S * H;
-  if (sh == 0 || t == 0) return cudaSuccess;
-  switch (in_code) {
-    case kBF16:
-      return prep_dispatch_out(stream, static_cast<const __nv_bfloat16*>(x), lx, out, out_code, sh, H, t, p);
-    case kF16: return prep_dispatch_out(stream, static_cast<const __half*>(x), lx, out, out_code, sh, H, t, p);
-    default: return prep_dispatch_out(stream, static_cast<const float*>(x), lx, out, out_code, sh, H, t, p);
-  }
+  PrepJob job{x, lx, out, p};
+  return launch_qk_prep(stream, in_code, out_code, S, H, t, &job, 1);
 }
 
 cudaError_t launch_layernorm(cudaStream_t stream, const void* x, void* out, int code, const float* w, const float* b,

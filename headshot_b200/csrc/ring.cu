@@ -307,22 +307,21 @@ hs_status hs_ring_attention_fused(hs_ring* ring, const void* q, const void* k, c
     kp.norm2_max = ring->norm2 + 1;
     qp.norm2_max = ring->norm2;
   }
-  {
-    hs::ProfScope prof(ctx, st, "qk_prep");
-    e = bounded ? hs::launch_qk_prep(st, k, code, hs::RowLayout::head_major(H, tr), b0, code, 1, H, tr, kp)
-                : cudaMemcpyAsync(b0, k, rows * row_bytes, cudaMemcpyDeviceToDevice, st);
-  }
-  if (e != cudaSuccess) return hs::abi_cuda_fail(e, "ring K' prep");
-  e = cudaMemcpyAsync(b0 + rows * row_bytes, v, rows * row_bytes, cudaMemcpyDeviceToDevice, st);
-  if (e != cudaSuccess) return hs::abi_cuda_fail(e, "ring V copy");
-  if (bounded) {
+  const hs::RowLayout hm = hs::RowLayout::head_major(H, tr);
+  if (bounded) {  // K' into block 0 and Q' into the state buffer, one launch
+    const hs::PrepJob jobs[2] = {{k, hm, b0, kp}, {q, hm, ring->state, qp}};
     {
       hs::ProfScope prof(ctx, st, "qk_prep");
-      e = hs::launch_qk_prep(st, q, code, hs::RowLayout::head_major(H, tr), ring->state, code, 1, H, tr, qp);
+      e = hs::launch_qk_prep(st, code, code, 1, H, tr, jobs, 2);
     }
-    if (e != cudaSuccess) return hs::abi_cuda_fail(e, "ring Q' prep");
+    if (e != cudaSuccess) return hs::abi_cuda_fail(e, "ring Q'/K' prep");
     q_use = ring->state;
+  } else {
+    e = cudaMemcpyAsync(b0, k, rows * row_bytes, cudaMemcpyDeviceToDevice, st);
+    if (e != cudaSuccess) return hs::abi_cuda_fail(e, "ring K copy");
   }
+  e = cudaMemcpyAsync(b0 + rows * row_bytes, v, rows * row_bytes, cudaMemcpyDeviceToDevice, st);
+  if (e != cudaSuccess) return hs::abi_cuda_fail(e, "ring V copy");
   cudaEventRecord(ring->ev_block0, st);
   if (bounded) {
     cudaStreamWaitEvent(cs, ring->ev_block0, 0);

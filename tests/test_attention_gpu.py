@@ -302,3 +302,25 @@ def test_block_fused_f32_storage(gpu_ctx):
     gpu_ctx.sync()
     assert out.dtype == torch.float32
     gate(host(out), ref)
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+def test_repeated_calls_are_bit_identical(gpu_ctx, dtype):
+    # The kernel's barriers must not depend on timing: warps of a warpgroup
+    # drift apart by up to a tile (the last tile's epilogue once read O
+    # early when a fast warp got there before the item's second-to-last PV
+    # product was issued).  Many identical calls, all equal bit for bit.
+    s, h, t, d, prefix, eps = 2, 16, 1374, 64, 5, 1e-6
+    rng = np.random.default_rng(123)
+    q, k, v = (rounded(rng.standard_normal((s, h, t, d), np.float32), dtype) for _ in range(3))
+    qw, kw = (rng.uniform(0.8, 1.6, d).astype(np.float32) for _ in range(2))
+    qb, kb = (rng.uniform(-0.1, 0.1, d).astype(np.float32) for _ in range(2))
+    sin, cos = oracle.rope_tables(37, 37)
+    c = lambda a: torch.from_numpy(a).cuda()  # noqa: E731
+    norm, rope = QkNorm(c(qw), c(qb), c(kw), c(kb), eps), Rope(c(sin), c(cos), prefix, t)
+    qd, kd, vd = (dev(x, dtype) for x in (q, k, v))
+    first = gpu_ctx.attention_fused(qd, kd, vd, qk_norm=norm, rope=rope)
+    for i in range(64):
+        again = gpu_ctx.attention_fused(qd, kd, vd, qk_norm=norm, rope=rope)
+        gpu_ctx.sync()
+        assert torch.equal(first, again), f"call {i + 1} differs from the first"
