@@ -52,6 +52,10 @@ WORKLOADS = {
 }
 
 
+# DRAM bytes (read + write) per attention launch, one-pass ncu captures.
+MEASURED_TRAFFIC = {"global": 12.26e9 + 574.90e6, "global43k": 271.62e6 + 74.69e6}
+
+
 def log(*a):
     print(*a, file=sys.stderr, flush=True)
 
@@ -386,17 +390,16 @@ def run_ours(args, wl: dict, rank: int, world: int, local: int) -> dict | None:
     attn_per_launch_ms = attn_ms / max(attn_n, 1)
     flops_per_launch = flops_rank if session is None else flops_rank / world
     achieved = flops_per_launch / (attn_per_launch_ms / 1e3) / 1e12
-    # DRAM bytes per launch: the ncu capture of the 43,968-token global launch
-    # (profiles/attn_fwd_sm100_global43k_full.md) read+wrote 344.6 MB = 489.9 B
-    # per (token, head); K/V of one head stay L2-resident up to this config, so
-    # the traffic scales with the launch's (token, head) count.
+    # DRAM bytes per attention launch from one-pass ncu captures of these
+    # exact single-GPU launches (dram__bytes_read.sum + dram__bytes_write.sum;
+    # profiles/attn_fwd_sm100_dram_traffic.md).  Not captured for the other
+    # workloads or for ring steps: null there.
     traffic = None
-    if S == 1:
-        traffic = int(round(344.62e6 / (43968 * 16) * (T / world) * H))
+    if world == 1 and args.workload in MEASURED_TRAFFIC:
+        traffic = int(MEASURED_TRAFFIC[args.workload])
     roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peaks["bf16"], "unit": "TFLOP/s",
                 "frac": round(achieved / peaks["bf16"], 4), "traffic": traffic,
-                "traffic_source": "ncu dram__bytes_read+write of the 43,968-token launch, scaled by tokens"
-                if traffic else None,
+                "traffic_source": "ncu dram__bytes_read+write of this launch (1 pass)" if traffic else None,
                 "peak_source": f"{peaks['source']} bf16 burst (MEASURED_PEAKS.json)",
                 "kernel": "attn_fwd_sm100", "kernel_ms_per_launch": round(attn_per_launch_ms, 3),
                 "launches": attn_n, "kernel_share_of_step": round(attn_ms / max(all_ms, 1e-9), 4)}
