@@ -439,6 +439,37 @@ hs_status hs_attention_fused(hs_ctx* ctx, const void* q, const void* k, const vo
   return attention_impl(ctx, q, k, v, out, S, H, T, D, dtype, scale, qp, kp, name);
 }
 
+hs_status hs_linear(hs_ctx* ctx, const void* x, const void* w, const float* bias, void* out, uint64_t M, uint32_t K,
+                    uint32_t N, hs_dtype dtype, int epilogue, const void* residual, const float* gamma) {
+  const char* name = "hs_linear";
+  if (!ctx) return fail(HS_ERR_INVALID, std::string(name) + ": null context");
+  if (!valid_dtype(dtype)) return fail(HS_ERR_INVALID, std::string(name) + ": unknown dtype");
+  if (M == 0 || N == 0) return HS_OK;
+  if (dtype == HS_F32)
+    return fail(HS_ERR_UNSUPPORTED, std::string(name) + ": f32 storage is not implemented (f16/bf16 only)");
+  if (K == 0 || K % 8 || N % 8)
+    return fail(HS_ERR_UNSUPPORTED, std::string(name) + ": K and N must be non-zero multiples of 8 (16-byte rows)");
+  if (epilogue < HS_LINEAR_PLAIN || epilogue > HS_LINEAR_RESIDUAL_LS)
+    return fail(HS_ERR_INVALID, std::string(name) + ": unknown epilogue");
+  if (!x || !w || !out) return fail(HS_ERR_INVALID, std::string(name) + ": null tensor pointer");
+  if (epilogue == HS_LINEAR_RESIDUAL_LS && (!residual || !gamma))
+    return fail(HS_ERR_INVALID, std::string(name) + ": the residual epilogue needs residual and gamma");
+  if (!aligned16(x) || !aligned16(w) || !aligned16(out) || (residual && !aligned16(residual)))
+    return fail(HS_ERR_INVALID, std::string(name) + ": tensor pointers must be 16-byte aligned");
+  DeviceGuard guard(ctx->device);
+  cudaStream_t st = ctx_stream(ctx);
+  const int elem = dtype == HS_F16 ? kF16 : kBF16;
+  std::string err;
+  cudaError_t e;
+  {
+    ProfScope prof(ctx, st, "linear");
+    e = launch_linear_sm100(st, elem, x, w, bias, out, M, K, N, epilogue, residual, gamma, ctx->d_status,
+                            ctx_timeout_ns(ctx), &err);
+  }
+  if (e != cudaSuccess) return fail(HS_ERR_CUDA, std::string(name) + ": " + (err.empty() ? cudaGetErrorString(e) : err));
+  return HS_OK;
+}
+
 hs_status hs_attention_block_fused(hs_ctx* ctx, const void* q, const void* k, const void* v, void* out, uint32_t S,
                                    uint32_t T, uint32_t H, uint32_t D, hs_dtype dtype, float scale,
                                    const float* q_norm_w, const float* q_norm_b, const float* k_norm_w,

@@ -90,6 +90,16 @@ cudaError_t launch_attention_sm100(cudaStream_t stream, int elem, const AttnIO& 
                                    uint64_t timeout_ns, std::string* err);
 
 // Row prep for K (and for casts): out = RoPE(LN(x)) in `out_code` storage.
+// Epilogues of the block's linears (gemm_sm100.cu).
+enum LinearEpilogue : int { kEpiNone = 0, kEpiGelu = 1, kEpiResidual = 2 };
+
+// out (m, n) = x (m, k) . w (n, k)^T [+ bias] then the epilogue, 16-bit
+// `elem` storage, f32 accumulation; k and n multiples of 8, 16-byte
+// aligned rows.  kEpiResidual reads res (m, n) and gamma (n).
+cudaError_t launch_linear_sm100(cudaStream_t stream, int elem, const void* x, const void* w, const float* bias,
+                                void* out, uint64_t m, uint32_t k, uint32_t n, int epi, const void* res,
+                                const float* gamma, int* status, uint64_t timeout_ns, std::string* err);
+
 // One tensor of a qk_prep launch: x (S, H, T, 64) in layout `lx` in, head-
 // major rows out, with its own prologue.
 struct PrepJob {

@@ -176,6 +176,40 @@ class GpuContext:
             0.0 if scale is None else float(scale), *pro))
         return out
 
+    _EPILOGUES = {"none": 0, "gelu": 1, "residual_ls": 2}
+
+    def linear(self, x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None,
+               epilogue: str = "none", residual: torch.Tensor | None = None, gamma: torch.Tensor | None = None,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+        """out (M, N) = x (M, K) @ weight (N, K)^T [+ bias] (ops.rs:87-128), then the fused
+        epilogue: "gelu" (block.rs:173-174) or "residual_ls": residual + gamma * out
+        (ops.rs:168-183)."""
+        k = x.shape[-1]
+        m = x.numel() // k
+        assert weight.dim() == 2 and weight.shape[1] == k, "weight k mismatch"
+        assert weight.dtype == x.dtype, "weight/activation dtype"
+        n = weight.shape[0]
+        self._check_tensor(x, "x")
+        self._check_tensor(weight, "weight")
+        if bias is not None:
+            assert bias.numel() == n, "bias len"
+            assert bias.dtype == torch.float32, "bias must be f32"
+            self._check_tensor(bias, "bias")
+        epi = self._EPILOGUES[epilogue]
+        if epi == 2:
+            assert residual is not None and gamma is not None, "residual_ls needs residual and gamma"
+            assert residual.numel() == m * n and residual.dtype == x.dtype
+            assert gamma.dtype == torch.float32 and gamma.numel() == n, "gamma must be f32 (N)"
+            self._check_tensor(residual, "residual")
+            self._check_tensor(gamma, "gamma")
+        if out is None:
+            out = torch.empty((*x.shape[:-1], n), dtype=x.dtype, device=x.device)
+        assert out.numel() == m * n and out.dtype == x.dtype
+        self._bind_stream()
+        check(self._L.hs_linear(self._h, _ptr(x), _ptr(weight), _ptr(bias), _ptr(out), m, k, n, _code(x), epi,
+                                _ptr(residual), _ptr(gamma)))
+        return out
+
     def layernorm(self, x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:
         """Row LayerNorm over the last dim, f32 statistics (ops.rs:130-153; the reference fixes eps 1e-5)."""
         dim = x.shape[-1]

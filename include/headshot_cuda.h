@@ -169,6 +169,24 @@ HS_API hs_status hs_attention_fused_noalloc(void* stream, int* status, const voi
                                             float eps, const float* rope_sin, const float* rope_cos,
                                             uint32_t rope_rows, uint32_t prefix, uint32_t tokens_per_frame);
 
+/* Replaces GpuContext::linear (src/engine/ops.rs:87-128) and fuses the
+ * element-wise op that follows each linear in Block::forward:
+ *   out (M, N) = x (M, K) . w (N, K)^T [+ bias (N, f32)], then
+ *   HS_LINEAR_PLAIN       nothing                      (qkv projections)
+ *   HS_LINEAR_GELU        erf GELU (shaders/gelu.wesl) (MLP fc1 + gelu, block.rs:173-174)
+ *   HS_LINEAR_RESIDUAL_LS out = residual + gamma (.) out (proj/fc2 + residual_ls,
+ *                         shaders/residual_ls.wesl); residual (M, N), gamma (N, f32).
+ * f16/bf16 storage on tcgen05 with f32 accumulation (the fused epilogue
+ * works on the f32 sum; the reference rounds the linear's output first).
+ * K and N must be multiples of 8; f32 storage returns HS_ERR_UNSUPPORTED.
+ * bias may be NULL.  out may alias residual. */
+#define HS_LINEAR_PLAIN 0
+#define HS_LINEAR_GELU 1
+#define HS_LINEAR_RESIDUAL_LS 2
+HS_API hs_status hs_linear(hs_ctx* ctx, const void* x, const void* w, const float* bias, void* out, uint64_t M,
+                           uint32_t K, uint32_t N, hs_dtype dtype, int epilogue, const void* residual,
+                           const float* gamma);
+
 /* Replaces GpuContext::layernorm (src/engine/ops.rs:130-153), with eps an
  * argument (the reference fixes 1e-5, ops.rs:139).  w, b: (dim) f32. */
 HS_API hs_status hs_layernorm(hs_ctx* ctx, const void* x, const float* w, const float* b, void* out, uint64_t rows,

@@ -61,6 +61,9 @@ def lib() -> ctypes.CDLL:
         L.or_attention.restype = ctypes.c_int
         L.or_attention_rows.argtypes = [_f32p, _f32p, _f32p, _f32p, u32, u32, f32, _i64p, u64, ctypes.c_int]
         L.or_attention_rows.restype = ctypes.c_int
+        L.or_linear.argtypes = [_f32p, _f32p, _f32p, _f32p, u64, u32, u32, ctypes.c_int]
+        L.or_gelu.argtypes = [_f32p, _f32p, u64]
+        L.or_residual_ls.argtypes = [_f32p, _f32p, _f32p, _f32p, u64, u32]
         _lib = L
     return _lib
 
@@ -201,6 +204,34 @@ def attention_rows(q, k, v, rows, scale: float | None = None, nthreads: int | No
 
 
 # --------------------------------------------------------- parity gate ----
+
+def linear(x: np.ndarray, w: np.ndarray, b: np.ndarray | None = None, nthreads: int | None = None) -> np.ndarray:
+    """out (M, N) = x (M, K) . w (N, K)^T [+ b] (shaders/linear.wesl)."""
+    x, w = _f32(x), _f32(w)
+    K = x.shape[-1]
+    M = x.size // K
+    N = w.shape[0]
+    assert w.shape == (N, K)
+    out = np.empty((M, N), np.float32)
+    lib().or_linear(_p(x), _p(w), None if b is None else _p(_f32(b)), _p(out), M, K, N, nthreads or threads())
+    return out
+
+
+def gelu(x: np.ndarray) -> np.ndarray:
+    """Erf GELU, erf by A&S 7.1.26 (shaders/gelu.wesl)."""
+    x = _f32(x)
+    out = np.empty_like(x)
+    lib().or_gelu(_p(x), _p(out), x.size)
+    return out
+
+
+def residual_ls(res: np.ndarray, x: np.ndarray, gamma: np.ndarray) -> np.ndarray:
+    """res + gamma * x over the last dim (shaders/residual_ls.wesl)."""
+    res, x, gamma = _f32(res), _f32(x), _f32(gamma)
+    out = np.empty_like(x)
+    lib().or_residual_ls(_p(res), _p(x), _p(gamma), _p(out), x.size, gamma.size)
+    return out
+
 
 def compare(ours: np.ndarray, ref: np.ndarray) -> dict:
     """src/parity.rs:35-60: max_abs, mean_abs, cosine, ref_scale in f64."""

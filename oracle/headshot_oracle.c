@@ -19,6 +19,9 @@
  *   or_split_heads      shaders/split_heads.wesl:27-41
  *   or_attn_merge       shaders/attn_merge.wesl:23-36
  *   or_rng_uniform      tests/kernels.rs:7-23          (SplitMix64 -> [-1,1])
+ *   or_linear           shaders/linear.wesl            (x . w^T, f32 accumulation in k order, + bias)
+ *   or_gelu             shaders/gelu.wesl:16-35        (erf by Abramowitz & Stegun 7.1.26)
+ *   or_residual_ls      shaders/residual_ls.wesl       (res + gamma * x)
  *
  * Extension beyond the reference (documented, identity when unused):
  * or_rope_apply takes `tokens_per_frame`; the table row of token t is
@@ -350,4 +353,69 @@ OR_API int or_attention(const float *q, const float *k, const float *v, float *o
 OR_API int or_attention_rows(const float *q, const float *k, const float *v, float *out, uint32_t T,
                              uint32_t D, float scale, const int64_t *rows, uint64_t nrows, int nthreads) {
     return run_rows(q, k, v, out, rows, nrows, T, D, scale, nthreads);
+}
+
+/* ---------------------------------------------------------------- linear --
+ * out (M,N) = x (M,K) . w (N,K)^T [+ bias]: f32 sum over k in increasing
+ * order per output, bias added after the sum (linear.wesl's 16-wide tiles
+ * walk k in the same order).  Rows split across threads. */
+typedef struct {
+    const float *x, *w, *bias;
+    float *out;
+    uint64_t m0, m1;
+    uint32_t K, N;
+} lin_job;
+
+static void *lin_worker(void *arg) {
+    const lin_job *j = (const lin_job *)arg;
+    for (uint64_t r = j->m0; r < j->m1; ++r) {
+        const float *xr = j->x + r * j->K;
+        for (uint32_t c = 0; c < j->N; ++c) {
+            const float *wc = j->w + (uint64_t)c * j->K;
+            float acc = 0.0f;
+            for (uint32_t k = 0; k < j->K; ++k) acc += xr[k] * wc[k];
+            if (j->bias) acc += j->bias[c];
+            j->out[r * j->N + c] = acc;
+        }
+    }
+    return NULL;
+}
+
+OR_API void or_linear(const float *x, const float *w, const float *bias, float *out, uint64_t M, uint32_t K,
+                      uint32_t N, int nthreads) {
+    if (nthreads < 1) nthreads = 1;
+    if (nthreads > 256) nthreads = 256;
+    if ((uint64_t)nthreads > M) nthreads = (int)(M ? M : 1);
+    pthread_t tid[256];
+    lin_job jobs[256];
+    for (int t = 0; t < nthreads; ++t) {
+        jobs[t] = (lin_job){x, w, bias, out, M * t / nthreads, M * (t + 1) / nthreads, K, N};
+    }
+    if (nthreads == 1) {
+        lin_worker(&jobs[0]);
+        return;
+    }
+    for (int t = 0; t < nthreads; ++t) pthread_create(&tid[t], NULL, lin_worker, &jobs[t]);
+    for (int t = 0; t < nthreads; ++t) pthread_join(tid[t], NULL);
+}
+
+/* GELU(v) = 0.5 v (1 + erf(v / sqrt 2)) with erf from Abramowitz & Stegun
+ * 7.1.26 (max abs error 1.5e-7), in f32 as gelu.wesl evaluates it. */
+static float erf_as(float v) {
+    const float s = v < 0.0f ? -1.0f : (v > 0.0f ? 1.0f : 0.0f);
+    const float a = fabsf(v);
+    const float t = 1.0f / (1.0f + 0.3275911f * a);
+    const float y = 1.0f - (((((1.061405429f * t - 1.453152027f) * t) + 1.421413741f) * t - 0.284496736f) * t +
+                            0.254829592f) * t * expf(-a * a);
+    return s * y;
+}
+
+OR_API void or_gelu(const float *x, float *out, uint64_t n) {
+    for (uint64_t i = 0; i < n; ++i) out[i] = 0.5f * x[i] * (1.0f + erf_as(x[i] * 0.7071067811865475f));
+}
+
+/* out[r, c] = res[r, c] + gamma[c] * x[r, c]. */
+OR_API void or_residual_ls(const float *res, const float *x, const float *gamma, float *out, uint64_t total,
+                           uint32_t dim) {
+    for (uint64_t i = 0; i < total; ++i) out[i] = res[i] + gamma[i % dim] * x[i];
 }

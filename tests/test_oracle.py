@@ -164,3 +164,37 @@ def test_gate_is_nan_proof():
         oracle.gate(oracle.compare(np.full(4, np.nan, np.float32), a))
     with pytest.raises(AssertionError):
         oracle.gate(oracle.compare(-a, a))
+
+
+# ---- block linears (f2): restatements of linear.wesl, gelu.wesl, residual_ls.wesl ----
+
+def test_linear_matches_reference_known_answer():
+    # tests/kernels.rs:63-98: Rng(2), (m, k, n) = (37, 53, 29), f64 reference, tol 1e-4
+    # (abs + rel, kernels.rs:35-43), with and without bias.
+    m, k, n = 37, 53, 29
+    vals = oracle.rng_uniform(2, m * k + n * k + n)
+    x = vals[:m * k].reshape(m, k)
+    w = vals[m * k:m * k + n * k].reshape(n, k)
+    b = vals[m * k + n * k:]
+    exp = (x.astype(np.float64) @ w.astype(np.float64).T).astype(np.float32) + b
+    got = oracle.linear(x, w, b)
+    assert np.all(np.abs(got - exp) <= 1e-4 + 1e-4 * np.abs(exp))
+    got = oracle.linear(x, w)
+    exp_nb = exp - b
+    assert np.all(np.abs(got - exp_nb) <= 1e-4 + 1e-4 * np.abs(exp_nb))
+
+
+def test_gelu_matches_erf_known_answer():
+    # tests/kernels.rs:128-147: x in [-8, 8] step 0.2, within 1e-5 of the exact erf GELU.
+    import math
+    xs = (np.arange(-40, 41) * 0.2).astype(np.float32)
+    got = oracle.gelu(xs)
+    exact = np.array([0.5 * v * (1 + math.erf(v / math.sqrt(2))) for v in xs.astype(np.float64)])
+    assert np.abs(got - exact).max() < 1e-5
+
+
+def test_residual_ls():
+    rng = np.random.default_rng(4)
+    res, x = (rng.standard_normal((7, 12)).astype(np.float32) for _ in range(2))
+    g = rng.standard_normal(12).astype(np.float32)
+    assert np.array_equal(oracle.residual_ls(res, x, g), res + g * x)
