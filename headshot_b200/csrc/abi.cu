@@ -454,8 +454,9 @@ hs_status hs_linear(hs_ctx* ctx, const void* x, const void* w, const float* bias
   if (!x || !w || !out) return fail(HS_ERR_INVALID, std::string(name) + ": null tensor pointer");
   if (epilogue == HS_LINEAR_RESIDUAL_LS && (!residual || !gamma))
     return fail(HS_ERR_INVALID, std::string(name) + ": the residual epilogue needs residual and gamma");
-  if (!aligned16(x) || !aligned16(w) || !aligned16(out) || (residual && !aligned16(residual)))
-    return fail(HS_ERR_INVALID, std::string(name) + ": tensor pointers must be 16-byte aligned");
+  if (!aligned16(x) || !aligned16(w) || !aligned16(out) || (residual && !aligned16(residual)) ||
+      (bias && !aligned16(bias)) || (gamma && !aligned16(gamma)))
+    return fail(HS_ERR_INVALID, std::string(name) + ": tensor and bias/gamma pointers must be 16-byte aligned");
   DeviceGuard guard(ctx->device);
   cudaStream_t st = ctx_stream(ctx);
   const int elem = dtype == HS_F16 ? kF16 : kBF16;

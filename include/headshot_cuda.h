@@ -179,7 +179,7 @@ HS_API hs_status hs_attention_fused_noalloc(void* stream, int* status, const voi
  * f16/bf16 storage on tcgen05 with f32 accumulation (the fused epilogue
  * works on the f32 sum; the reference rounds the linear's output first).
  * K and N must be multiples of 8; f32 storage returns HS_ERR_UNSUPPORTED.
- * bias may be NULL.  out may alias residual. */
+ * All pointers 16-byte aligned; bias may be NULL.  out may alias residual. */
 #define HS_LINEAR_PLAIN 0
 #define HS_LINEAR_GELU 1
 #define HS_LINEAR_RESIDUAL_LS 2
