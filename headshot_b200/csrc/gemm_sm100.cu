@@ -17,7 +17,9 @@
 //   warp 1      UMMA issue (whole warp, elect.sync): M=128, N=256, K=16, f32 in TMEM
 //   warp 2      TMEM owner (512 columns = two 256-column accumulators)
 //   warps 4-11  two epilogue warpgroups: one thread per output row of the
-//               tile, each warpgroup taking half of the tile's 256 columns
+//               tile, each warpgroup taking half of the tile's 256 columns;
+//               each warp stages its 32x32 output blocks in shared memory
+//               and writes them with TMA stores (coalesced, asynchronous)
 // The accumulator is double-buffered, so the epilogue of tile i overlaps the
 // MMAs of tile i+1.  Every wait is bounded (hs_ptx.cuh) and every waiter
 // waits completions in order.
@@ -65,7 +67,9 @@ struct Ctrl {
   int no_abort;
 };
 
-constexpr size_t kSmemBytes = 1024 + kStages * (kATileBytes + kBTileBytes) + sizeof(Ctrl);
+constexpr int kStageOutBytes = 32 * 32 * 2;  // one warp's 32x32 16-bit output block
+constexpr size_t kSmemBytes =
+    1024 + kStages * (kATileBytes + kBTileBytes) + kEpiWarps * 2 * kStageOutBytes + sizeof(Ctrl);
 static_assert(kSmemBytes <= 232448, "shared memory per CTA");
 
 struct Args {
@@ -88,17 +92,47 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
   return __all_sync(0xffffffffu, r);
 }
 
-// erf by Abramowitz & Stegun 7.1.26 (|error| <= 1.5e-7), the formula the
-// reference's GELU kernel uses (shaders/gelu.wesl:16-26).  The fast
-// reciprocal and exponential intrinsics keep the epilogue short; their
-// relative error (~1e-6) is far below the 16-bit output rounding.
-__device__ __forceinline__ float gelu_erf(float v) {
-  const float x = v * 0.70710678118654752f;
-  const float a = fabsf(x);
-  const float t = __frcp_rn(1.0f + 0.3275911f * a);
-  const float poly = ((((1.061405429f * t - 1.453152027f) * t + 1.421413741f) * t - 0.284496736f) * t + 0.254829592f) * t;
-  const float e = 1.0f - poly * __expf(-a * a);
-  return 0.5f * v * (1.0f + copysignf(e, x));
+// Packed f32x2 arithmetic (sm_100).
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 splat(float v) { return make_float2(v, v); }
+
+// GELU(v) = 0.5 v (1 + erf(v / sqrt 2)) on a pair, erf by Abramowitz &
+// Stegun 7.1.26 (|error| <= 1.5e-7), the formula the reference's GELU kernel
+// uses (shaders/gelu.wesl:16-26).  The fast reciprocal and exponential
+// intrinsics keep the epilogue short; their relative error (~1e-6) is far
+// below the 16-bit output rounding.
+__device__ __forceinline__ float2 gelu_erf2(float2 v) {
+  const float2 x = mul2(v, splat(0.70710678118654752f));
+  const float2 a = make_float2(fabsf(x.x), fabsf(x.y));
+  const float2 d = fma2(a, splat(0.3275911f), splat(1.0f));
+  const float2 t = make_float2(__frcp_rn(d.x), __frcp_rn(d.y));
+  float2 p = fma2(t, splat(1.061405429f), splat(-1.453152027f));
+  p = fma2(p, t, splat(1.421413741f));
+  p = fma2(p, t, splat(-0.284496736f));
+  p = fma2(p, t, splat(0.254829592f));
+  p = mul2(p, t);
+  const float2 q = mul2(a, make_float2(-a.x, -a.y));
+  const float2 ex = make_float2(__expf(q.x), __expf(q.y));
+  const float2 e = fma2(make_float2(-p.x, -p.y), ex, splat(1.0f));
+  const float2 h = mul2(v, splat(0.5f));
+  return fma2(h, make_float2(copysignf(e.x, x.x), copysignf(e.y, x.y)), h);
 }
 
 // 32 consecutive f32 values of a per-column vector (bias, gamma), or zeros.
@@ -177,12 +211,15 @@ __device__ void mma_role(const Args& a, uint8_t* sA, uint8_t* sB, Ctrl* ctl, uin
 }
 
 template <typename E>
-__device__ void epilogue_role(const Args& a, Ctrl* ctl, uint32_t tmem, int warp, int lane) {
+__device__ void epilogue_role(const Args& a, const CUtensorMap* tm_out, uint8_t* sOut, Ctrl* ctl, uint32_t tmem,
+                              int warp, int lane) {
   volatile int* abort_flag = &ctl->abort_flag;
   const int wq = (warp - kEpiWarp0) & 3;                  // TMEM lane quadrant of this warp
   const uint32_t col_base = ((warp - kEpiWarp0) >> 2) * kEpiCols;  // this warpgroup's columns
   const uint32_t row_in_tile = static_cast<uint32_t>(wq * 32 + lane);
   const uint32_t lane_base = static_cast<uint32_t>(wq * 32) << 16;
+  uint8_t* stage_base = sOut + (warp - kEpiWarp0) * 2 * kStageOutBytes;
+  uint32_t blocks = 0;  // output blocks this warp has stored (alternating staging buffers)
   uint32_t i = 0;
   for (uint32_t tile = blockIdx.x; tile < a.n_tiles_total; tile += gridDim.x, ++i) {
     const uint32_t ab = i & 1;
@@ -197,15 +234,19 @@ __device__ void epilogue_role(const Args& a, Ctrl* ctl, uint32_t tmem, int warp,
       uint32_t acc[32];
       tmem_ld32(tmem + lane_base + ab * kBN + col_base + 32 * c, acc);
       tmem_wait_ld_regs<32>(acc);
-      if (!row_ok || col0 >= a.n) continue;
+      if (col0 >= a.n || row - lane >= a.m) continue;  // warp-uniform: nothing of this block is stored
       float v[32];
       load_cols32(a.bias, col0, a.n, v);
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] += __uint_as_float(acc[j]);
       if (a.epi == kEpiGelu) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
-      } else if (a.epi == kEpiResidual) {
+        for (int j = 0; j < 32; j += 2) {
+          const float2 r = gelu_erf2(make_float2(v[j], v[j + 1]));
+          v[j] = r.x;
+          v[j + 1] = r.y;
+        }
+      } else if (a.epi == kEpiResidual && row_ok) {
         const E* res = static_cast<const E*>(a.res) + row * a.n + col0;
         float g[32];
         load_cols32(a.gamma, col0, a.n, g);
@@ -223,33 +264,50 @@ __device__ void epilogue_role(const Args& a, Ctrl* ctl, uint32_t tmem, int warp,
           }
         }
       }
-      E* dst = static_cast<E*>(a.out) + row * a.n + col0;
+      // Stage this warp's 32 rows x 32 columns (row = lane) and store the
+      // block with one TMA store; rows past M and columns past N are clipped.
+      uint8_t* stage = stage_base + (blocks & 1) * kStageOutBytes;
+      if (blocks >= 2) {
+        if (lane == 0) bulk_wait_group_read<1>();  // the store that used this buffer has read it
+        __syncwarp();
+      }
+      uint4* srow = reinterpret_cast<uint4*>(stage + lane * 64);
 #pragma unroll
       for (int j8 = 0; j8 < 4; ++j8) {
-        if (col0 + 8 * j8 >= a.n) break;  // N is a multiple of 8
         uint4 o;
         o.x = Elem<E>::pack2(v[8 * j8 + 0], v[8 * j8 + 1]);
         o.y = Elem<E>::pack2(v[8 * j8 + 2], v[8 * j8 + 3]);
         o.z = Elem<E>::pack2(v[8 * j8 + 4], v[8 * j8 + 5]);
         o.w = Elem<E>::pack2(v[8 * j8 + 6], v[8 * j8 + 7]);
-        reinterpret_cast<uint4*>(dst)[j8] = o;
+        srow[j8] = o;
       }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(tm_out, stage, static_cast<int>(col0), static_cast<int>(row - lane));
+        bulk_commit_group();
+      }
+      ++blocks;
     }
     // The accumulator may be overwritten once every warp has read it.
     tc_fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(&ctl->acc_empty[ab]);
   }
+  if (lane == 0) bulk_wait_group<0>();  // every store of this warp has landed before the CTA exits
+  __syncwarp();
 }
 
 template <typename E>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_sm100(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b, const Args a) {
+    gemm_sm100(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+               const __grid_constant__ CUtensorMap tm_out, const Args a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = sA + kStages * kATileBytes;
-  Ctrl* ctl = reinterpret_cast<Ctrl*>(sB + kStages * kBTileBytes);
+  uint8_t* sOut = sB + kStages * kBTileBytes;
+  Ctrl* ctl = reinterpret_cast<Ctrl*>(sOut + kEpiWarps * 2 * kStageOutBytes);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
@@ -270,6 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == kProducerWarp && lane == 0) {
     tma_prefetch_desc(&tm_a);
     tma_prefetch_desc(&tm_b);
+    tma_prefetch_desc(&tm_out);
   }
   if (warp == kTmemWarp) {
     tmem_alloc(&ctl->tmem_base, kTmemCols);
@@ -285,7 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == kMmaWarp) {
     mma_role<Elem<E>::kBf16>(a, sA, sB, ctl, tmem);
   } else if (warp >= kEpiWarp0) {
-    epilogue_role<E>(a, ctl, tmem, warp, lane);
+    epilogue_role<E>(a, &tm_out, sOut, ctl, tmem, warp, lane);
   }
   __syncwarp();
   tc_fence_before();
@@ -311,6 +370,28 @@ EncodeTiledFn encode_fn() {
       fn = reinterpret_cast<EncodeTiledFn>(p);
   });
   return fn;
+}
+
+// Row-major (rows, cols) 16-bit output as a 2-D map with 32x32 boxes, no
+// swizzle (the epilogue's staging layout).
+bool make_out_map(CUtensorMap* map, void* base, bool bf16, uint64_t rows, uint32_t cols, std::string* err) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) {
+    if (err) *err = "cuTensorMapEncodeTiled unavailable";
+    return false;
+  }
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, dims,
+                  strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    if (err) *err = "cuTensorMapEncodeTiled (output) failed with code " + std::to_string(static_cast<int>(r));
+    return false;
+  }
+  return true;
 }
 
 // Row-major (rows, cols) 16-bit matrix as a 3-D map (cols, rows, 1) with
@@ -351,8 +432,8 @@ int sm_count() {
 }
 
 template <typename E>
-cudaError_t launch_typed(cudaStream_t stream, const CUtensorMap& ma, const CUtensorMap& mb, const Args& a,
-                         uint32_t ctas) {
+cudaError_t launch_typed(cudaStream_t stream, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo,
+                         const Args& a, uint32_t ctas) {
   static bool configured = false;
   if (!configured) {
     cudaError_t e =
@@ -360,7 +441,7 @@ cudaError_t launch_typed(cudaStream_t stream, const CUtensorMap& ma, const CUten
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  gemm_sm100<E><<<ctas, kThreads, kSmemBytes, stream>>>(ma, mb, a);
+  gemm_sm100<E><<<ctas, kThreads, kSmemBytes, stream>>>(ma, mb, mo, a);
   return cudaGetLastError();
 }
 
@@ -371,8 +452,9 @@ cudaError_t launch_linear_sm100(cudaStream_t stream, int elem, const void* x, co
                                 const float* gamma, int* status, uint64_t timeout_ns, std::string* err) {
   if (m == 0 || n == 0) return cudaSuccess;
   const bool bf16 = elem == kBF16;
-  CUtensorMap ma, mb;
-  if (!make_map(&ma, x, bf16, m, k, kBM, err) || !make_map(&mb, w, bf16, n, k, kBN, err))
+  CUtensorMap ma, mb, mo;
+  if (!make_map(&ma, x, bf16, m, k, kBM, err) || !make_map(&mb, w, bf16, n, k, kBN, err) ||
+      !make_out_map(&mo, out, bf16, m, n, err))
     return cudaErrorInvalidValue;
   Args a{};
   a.out = out;
@@ -396,7 +478,8 @@ cudaError_t launch_linear_sm100(cudaStream_t stream, int elem, const void* x, co
   a.timeout_ns = timeout_ns;
   uint32_t ctas = static_cast<uint32_t>(sm_count());
   if (ctas > a.n_tiles_total) ctas = a.n_tiles_total;
-  return bf16 ? launch_typed<__nv_bfloat16>(stream, ma, mb, a, ctas) : launch_typed<__half>(stream, ma, mb, a, ctas);
+  return bf16 ? launch_typed<__nv_bfloat16>(stream, ma, mb, mo, a, ctas)
+              : launch_typed<__half>(stream, ma, mb, mo, a, ctas);
 }
 
 }  // namespace hs
