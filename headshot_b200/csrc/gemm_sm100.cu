@@ -122,7 +122,7 @@ __device__ __forceinline__ float2 gelu_erf2(float2 v) {
   const float2 x = mul2(v, splat(0.70710678118654752f));
   const float2 a = make_float2(fabsf(x.x), fabsf(x.y));
   const float2 d = fma2(a, splat(0.3275911f), splat(1.0f));
-  const float2 t = make_float2(__frcp_rn(d.x), __frcp_rn(d.y));
+  const float2 t = make_float2(__fdividef(1.0f, d.x), __fdividef(1.0f, d.y));
   float2 p = fma2(t, splat(1.061405429f), splat(-1.453152027f));
   p = fma2(p, t, splat(1.421413741f));
   p = fma2(p, t, splat(-0.284496736f));
