@@ -45,6 +45,11 @@ WORKLOADS = {
     # Same work as "frame" on the layout Block::forward hands over: q, k, v are the
     # (S*T, H*D) projection outputs and the output is the merged (S*T, H*D) tensor
     # (split_heads, QK-norm, RoPE, attention and attn_merge in one call).
+    # The block MLP of the aggregator (block.rs:167-176 + residual_ls) at BASELINE
+    # config 5's global-layer token count: fc1 + GELU, fc2 + LayerScale residual.
+    "mlp": dict(kind="mlp", tokens=137400, d=1024, hidden=4096, dtype="bf16", seed=5,
+                name="block MLP at 137,400 tokens (100 frames x 1374), d 1024, hidden 4096, bf16: "
+                     "fc1 + bias + erf-GELU, fc2 + bias + LayerScale residual (hs_linear)"),
     "frame_block": dict(S=200, H=16, frames=1, T_f=1374, dtype="f16", seed=2, prefix=5, grid=(37, 37), eps=1e-6,
                         layout="block",
                         name="batched frame attention on the projection layout (S*T, H*D) in and merged out, "
@@ -440,6 +445,153 @@ def run_ours(args, wl: dict, rank: int, world: int, local: int) -> dict | None:
     return result
 
 
+def run_mlp(args, wl: dict, rank: int, world: int, local: int) -> dict | None:
+    """Block MLP through hs_linear: rows sharded across ranks, no communication."""
+    import torch
+
+    from headshot_b200.engine import GpuContext
+    from headshot_b200.session import shard_bounds
+
+    tdt = {"bf16": torch.bfloat16, "f16": torch.float16}[wl["dtype"]]
+    ctx = GpuContext(local)
+    dev = torch.device("cuda", local)
+    r0, r1 = shard_bounds(wl["tokens"], world, rank)
+    m, d, hid = r1 - r0, wl["d"], wl["hidden"]
+    g = torch.Generator(device=dev).manual_seed(wl["seed"] * 1000 + rank)
+    x = torch.randn((m, d), device=dev, generator=g).to(tdt)  # LayerNorm'd block input
+    res = torch.randn((m, d), device=dev, generator=g).to(tdt)  # residual stream
+    w1 = (torch.randn((hid, d), device=dev, generator=g) * 0.02).to(tdt)
+    w2 = (torch.randn((d, hid), device=dev, generator=g) * 0.02).to(tdt)
+    b1 = torch.zeros(hid, device=dev)
+    b2 = torch.zeros(d, device=dev)
+    ls = torch.full((d,), 1e-5, device=dev)
+    hidden = torch.empty((m, hid), device=dev, dtype=tdt)
+    out = torch.empty((m, d), device=dev, dtype=tdt)
+
+    def step(xx=x, rr=res, oo=out):
+        ctx.linear(xx, w1, b1, epilogue="gelu", out=hidden)
+        ctx.linear(hidden, w2, b2, epilogue="residual_ls", residual=rr, gamma=ls, out=oo)
+
+    flops_rank = 2.0 * m * d * hid * 2
+    flops_total = 2.0 * wl["tokens"] * d * hid * 2
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        step()
+    ctx.sync()
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(gpu_id_for_smi(local))
+    sampler.start()
+    time.sleep(0.3)
+    ctx.prof_reset()
+    ctx.prof_enable(True)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    ctx.prof_enable(False)
+    clocks = sampler.stop()
+    ctx.sync()
+    ms = max_over_ranks(e0.elapsed_time(e1), world) / args.steps
+    lin_ms, lin_n = ctx.prof_read("linear")
+    value = flops_total / (ms / 1e3) / 1e12
+
+    # the same two layers unfused through cuBLAS and torch element-wise ops, for context
+    b1h, b2h, lsh = b1.to(tdt), b2.to(tdt), ls.to(tdt)
+
+    def unfused():
+        hh = torch.nn.functional.gelu(torch.nn.functional.linear(x, w1, b1h))
+        return res + lsh * torch.nn.functional.linear(hh, w2, b2h)
+
+    for _ in range(3):
+        unfused()
+    torch.cuda.synchronize(dev)
+    e0.record(stream)
+    for _ in range(args.steps):
+        unfused()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    unfused_ms = e0.elapsed_time(e1) / args.steps
+
+    # end to end: the step's input rows and residual up, the output down (pinned host memory)
+    xh, rh = x.cpu().pin_memory(), res.cpu().pin_memory()
+    oh = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+
+    def e2e_step():
+        ctx.upload(x, xh)
+        ctx.upload(res, rh)
+        step()
+        ctx.download(oh, out)
+
+    e2e_step()
+    torch.cuda.synchronize(dev)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ctx.sync()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world) / args.steps
+
+    peaks = measured_peaks()
+    achieved = flops_rank / (lin_ms / max(lin_n, 1) * 2 / 1e3) / 1e12  # two launches per step
+    result = None
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            cpu = cpu_mlp_sample(x, w1, w2, res, ls, args.cpu_threads or _threads())
+        result = {
+            "metric": "block MLP TFLOP/s (fc1+GELU, fc2+LayerScale residual) at 137,400 tokens",
+            "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": wl["dtype"], "data": f"synthetic N(0,1) rows, weights N(0, 0.02), seed {wl['seed']}",
+            "config": {"workload": wl["name"], "tokens": wl["tokens"], "d": d, "hidden": hid,
+                       "parallelism": f"row-sharded x{world}", "unfused_cublas_torch_ms": round(unfused_ms, 3),
+                       "l2": "inputs larger than L2 (x 281 MB, hidden 1.1 GB); no flush needed"},
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peaks["bf16"], "unit": "TFLOP/s",
+                         "frac": round(achieved / peaks["bf16"], 4), "traffic": None,
+                         "peak_source": f"{peaks['source']} bf16 burst (MEASURED_PEAKS.json)", "kernel": "gemm_sm100",
+                         "kernel_ms_per_launch": round(lin_ms / max(lin_n, 1), 3), "launches": lin_n},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(flops_total / (e2e_ms / 1e3) / 1e12, 2), "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": 2 * x.numel() * x.element_size() * world,
+                    "d2h_bytes_per_step": out.numel() * out.element_size() * world, "ms_per_step": round(e2e_ms, 3)},
+            "gpu_launches": int(lin_n) * world,
+            "clocks": clocks,
+        }
+    ctx.close()
+    return result
+
+
+def cpu_mlp_sample(x, w1, w2, res, ls, threads: int) -> dict:
+    """The reference path on the CPU (oracle linear.wesl + gelu.wesl + residual_ls.wesl) on a
+    bounded sample of rows (rows are independent)."""
+    import numpy as np
+
+    import oracle
+
+    w1h, w2h, lsh = w1.float().cpu().numpy(), w2.float().cpu().numpy(), ls.float().cpu().numpy()
+
+    def run(rows):
+        xs = x[:rows].float().cpu().numpy()
+        rs = res[:rows].float().cpu().numpy()
+        t0 = time.perf_counter()
+        hh = oracle.gelu(oracle.linear(xs, w1h, None, nthreads=threads))
+        oracle.residual_ls(rs, oracle.linear(hh, w2h, None, nthreads=threads), lsh)
+        return time.perf_counter() - t0
+
+    probe = max(run(4 * threads), 1e-3)  # size the sample at about 10 s of CPU work
+    rows = int(min(x.shape[0], max(4 * threads, 4 * threads * 10.0 / probe)))
+    dt = run(rows)
+    fl = 2.0 * rows * w1h.shape[1] * w1h.shape[0] * 2
+    return {"value": round(fl / dt / 1e12, 6), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{rows} token rows through fc1+GELU and fc2+residual, f32, {dt:.2f} s"}
+
+
 def _threads() -> int:
     return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
 
@@ -495,6 +647,43 @@ def run_reference(args, wl: dict) -> dict:
             "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+def run_reference_mlp(args, wl: dict) -> dict:
+    """The reference's CPU path for the block MLP (oracle restatements), bounded row samples."""
+    import numpy as np
+
+    import oracle
+
+    threads = args.cpu_threads or _threads()
+    rng = np.random.default_rng(wl["seed"])
+    d, hid = wl["d"], wl["hidden"]
+    w1 = oracle.round_to(wl["dtype"], (0.02 * rng.standard_normal((hid, d))).astype(np.float32))
+    w2 = oracle.round_to(wl["dtype"], (0.02 * rng.standard_normal((d, hid))).astype(np.float32))
+    ls = np.full(d, 1e-5, np.float32)
+    rows = 32 * threads
+    x = oracle.round_to(wl["dtype"], rng.standard_normal((rows, d)).astype(np.float32))
+    r = oracle.round_to(wl["dtype"], rng.standard_normal((rows, d)).astype(np.float32))
+
+    def step():
+        hh = oracle.gelu(oracle.linear(x, w1, None, nthreads=threads))
+        oracle.residual_ls(r, oracle.linear(hh, w2, None, nthreads=threads), ls)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = time.perf_counter() - t0
+    value = 2.0 * rows * d * hid * 2 * args.steps / dt / 1e12
+    return {"impl": "reference", "metric": "block MLP TFLOP/s (fc1+GELU, fc2+LayerScale residual) at 137,400 tokens",
+            "value": round(value, 6), "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": f"synthetic, seed {wl['seed']}, rounded to {wl['dtype']}",
+            "config": {"workload": wl["name"], "tokens": wl["tokens"], "d": d, "hidden": hid},
+            "cpu_baseline": {"value": round(value, 6), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                             "sample": f"{rows} token rows per step (rows are independent), f32 linear.wesl order"},
+            "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
 def _json_out():
     """The one JSON line goes to the original stdout; everything else written to
     file descriptor 1 during the run (NCCL prints its version banner there) is
@@ -527,14 +716,15 @@ def main():
         rank = int(os.environ.get("RANK", "0"))
         if rank != 0:
             return 0
-        print(json.dumps(run_reference(args, wl)), file=out, flush=True)
+        ref = run_reference_mlp(args, wl) if wl.get("kind") == "mlp" else run_reference(args, wl)
+        print(json.dumps(ref), file=out, flush=True)
         return 0
 
     rank, world, local = dist_setup()
     if world != args.gpus:
         log(f"note: --gpus {args.gpus} but WORLD_SIZE {world}; using {world}")
     try:
-        res = run_ours(args, wl, rank, world, local)
+        res = run_mlp(args, wl, rank, world, local) if wl.get("kind") == "mlp" else run_ours(args, wl, rank, world, local)
     finally:
         if world > 1:
             import torch.distributed as dist
