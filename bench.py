@@ -175,7 +175,7 @@ def dist_setup():
         torch.cuda.set_device(local)
         from datetime import timedelta
 
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
     else:
         torch.cuda.set_device(0)
     return rank, world, local

@@ -100,13 +100,13 @@ enum : int {
 };
 
 // Barrier phases are counted per barrier across all items of a CTA; every
-// waiter knows how many completions precede the one it wants.  Parity waits
-// cannot tell phase n from phase n+2 (nor n from n-2), so each barrier is
-// arranged such that its next completion needs an action of the waiter
-// taken after the wait, and every waiter waits the completions it needs in
-// order (never one two ahead of the last it saw): S buffers are doubled by
-// tile parity, PV-only batches at the end of an item complete pv_done
-// instead of an S buffer (the epilogue waits both), Q buffers are doubled.
+// waiter knows how many completions precede the one it wants.  A parity
+// wait cannot tell phase n from phase n +- 2, so every barrier is arranged
+// such that, when a waiter asks for completion k, completion k-1 has
+// already happened and completion k+1 needs an action the waiter takes
+// after this wait: S buffers are doubled by tile parity, Q buffers are
+// doubled, and the two PV products at the end of an item (no S behind
+// them) each complete a barrier of their own, once per item.
 struct Ctrl {
   uint64_t kv_full[kStages];      // K and V tile of a stage landed (one transaction count)
   uint64_t kv_empty[kStages];     // both MMA warps are done with the stage
@@ -114,7 +114,8 @@ struct Ctrl {
   uint64_t q_empty[2][kQBufs];    // the item's last QKᵀ product using that Q tile completed
   uint64_t s_full[2][2];          // [wg][buf]: S(j) landed (with PV(j-2) before it)
   uint64_t p_full[2][2];          // softmax wrote P (and rescaled O) for the tile in that buffer
-  uint64_t pv_done[2];            // a PV product with no S behind it (the last two of an item) completed
+  uint64_t pv_prev[2];            // PV(n-2) of the item completed (n >= 2)
+  uint64_t pv_last[2];            // PV(n-1) of the item completed (with every MMA before it)
   uint64_t drain[2];              // every MMA of that warpgroup's MMA warp completed
   uint64_t item_full[kItemSlots];   // the producer wrote an item index into the slot
   uint64_t item_empty[kItemSlots];  // every reader took it
@@ -273,13 +274,12 @@ __device__ void softmax_role(const Args& a, Ctrl* ctl, uint32_t tmem, int warp, 
   const float c = a.scale_log2;
   const uint32_t n = a.n_kv;
   const uint32_t tail = a.t_kv - (n - 1) * kBN;  // valid keys in the last tile, 1..kBN
-  // Completions per item: s_full[b] once per S tile with j % 2 == b,
-  // pv_done once per PV-only batch (the last min(n, 2) tiles).
-  // Only the parities of the completion counts before an item matter; they
-  // are packed into one register: bit 0 s_full[0], bit 1 s_full[1], bit 2
-  // pv_done.  Per item the counts grow by ceil(n/2), floor(n/2), min(n, 2).
-  const uint32_t step_bits = (((n + 1) >> 1) & 1) | (((n >> 1) & 1) << 1);  // pv_done grows by an even count
-  const uint32_t pv_last = n >= 2 ? 1 : 0;  // the epilogue waits the item's pv_done completion 1 + pv_last
+  // Completions per item: s_full[b] once per S tile with j % 2 == b;
+  // pv_prev and pv_last once each.  Only the parities of the completion
+  // counts before an item matter; they are packed into one register: bit 0
+  // s_full[0], bit 1 s_full[1], bit 2 pv_prev and pv_last.  Per item the
+  // counts grow by ceil(n/2), floor(n/2) and 1.
+  const uint32_t step_bits = (((n + 1) >> 1) & 1) | (((n >> 1) & 1) << 1) | 4u;
   uint32_t base_bits = 0;
   auto s_parity = [&](uint32_t t) { return ((base_bits >> (t & 1)) + (t >> 1)) & 1; };
 
@@ -387,7 +387,7 @@ __device__ void softmax_role(const Args& a, Ctrl* ctl, uint32_t tmem, int warp, 
         if (j > 0) {
           const bool ok = (j + 1 < n) ? warp_wait(&ctl->s_full[wg][(j + 1) & 1], s_parity(j + 1), abort_flag,
                                                   a.status, kSiteODone, a.timeout_ns)
-                                      : warp_wait(&ctl->pv_done[wg], (base_bits >> 2) & 1, abort_flag,
+                                      : warp_wait(&ctl->pv_prev[wg], (base_bits >> 2) & 1, abort_flag,
                                                   a.status, kSiteODone, a.timeout_ns);
           if (!ok) return;
           tc_fence_after();
@@ -411,18 +411,11 @@ __device__ void softmax_role(const Args& a, Ctrl* ctl, uint32_t tmem, int warp, 
       if (lane == 0) mbar_arrive(&ctl->p_full[wg][b]);
     }
 
-    // PV(n-1) is the item's last PV-only batch.  Wait for the item's
-    // pv_done completions in order: a warp that runs ahead of its
-    // warpgroup can get here before PV(n-2) has even been issued, and a
-    // parity wait for a completion two phases ahead would pass at once.
-    if (pv_last && !warp_wait(&ctl->pv_done[wg], (base_bits >> 2) & 1, abort_flag, a.status, kSiteODone,
-                              a.timeout_ns))
-      return;
-    if (!warp_wait(&ctl->pv_done[wg], ((base_bits >> 2) + pv_last) & 1, abort_flag, a.status, kSiteODone,
-                   a.timeout_ns))
+    // PV(n-1) and every MMA before it have completed: the item's pv_last.
+    if (!warp_wait(&ctl->pv_last[wg], (base_bits >> 2) & 1, abort_flag, a.status, kSiteODone, a.timeout_ns))
       return;
     tc_fence_after();
-    base_bits ^= step_bits | (pv_last ? 0u : 4u);
+    base_bits ^= step_bits;
 
     // ---- epilogue: O row from TMEM, normalise (or store the running state) --
 #pragma unroll
@@ -651,7 +644,7 @@ __device__ void mma_role(const Args& a, int wg, uint8_t* sQ, uint8_t* sK, uint8_
         umma_commit_elect(&ctl->s_full[wg][b]);
         if (j + 2 == n - 1) umma_commit_elect(&ctl->q_empty[wg][qb]);
       } else {
-        umma_commit_elect(&ctl->pv_done[wg]);
+        umma_commit_elect(j + 1 == n ? &ctl->pv_last[wg] : &ctl->pv_prev[wg]);
       }
       umma_commit_elect(&ctl->kv_empty[st]);  // the producer may refill this stage
     }
@@ -693,7 +686,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(&ctl->s_full[i][b], 1);
         mbar_init(&ctl->p_full[i][b], kBM / 32);
       }
-      mbar_init(&ctl->pv_done[i], 1);
+      mbar_init(&ctl->pv_prev[i], 1);
+      mbar_init(&ctl->pv_last[i], 1);
       mbar_init(&ctl->drain[i], 1);
     }
     for (int i = 0; i < kItemSlots; ++i) {
