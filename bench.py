@@ -50,6 +50,12 @@ WORKLOADS = {
     "mlp": dict(kind="mlp", tokens=137400, d=1024, hidden=4096, dtype="bf16", seed=5,
                 name="block MLP at 137,400 tokens (100 frames x 1374), d 1024, hidden 4096, bf16: "
                      "fc1 + bias + erf-GELU, fc2 + bias + LayerScale residual (hs_linear)"),
+    # Head-input cache build of one cached trunk layer at BASELINE config 5 (100 frames x
+    # 1374 tokens, C = 1024, bf16 -> f32 (N*T, 2048)), plus the register-layer gather and
+    # scatter of the 17 prefix tokens per frame (trunk.rs:105-140, cache.rs:25-52).
+    "trunk_glue": dict(kind="glue", frames=100, t=1374, c=1024, prefix=17, dtype="bf16", seed=6,
+                       name="trunk glue at 100 frames x 1374 tokens, C 1024, bf16: f32 head-input cache "
+                            "build (concat + cast) and the register gather/scatter"),
     "frame_block": dict(S=200, H=16, frames=1, T_f=1374, dtype="f16", seed=2, prefix=5, grid=(37, 37), eps=1e-6,
                         layout="block",
                         name="batched frame attention on the projection layout (S*T, H*D) in and merged out, "
@@ -567,6 +573,106 @@ def run_mlp(args, wl: dict, rank: int, world: int, local: int) -> dict | None:
     return result
 
 
+def run_glue(args, wl: dict, rank: int, world: int, local: int) -> dict | None:
+    """Cache build + register gather/scatter; frames sharded across ranks, no communication."""
+    import torch
+
+    from headshot_b200.engine import GpuContext
+    from headshot_b200.session import shard_bounds
+
+    tdt = {"bf16": torch.bfloat16, "f16": torch.float16}[wl["dtype"]]
+    ctx = GpuContext(local)
+    dev = torch.device("cuda", local)
+    f0, f1 = shard_bounds(wl["frames"], world, rank)
+    n, t, c, pre = f1 - f0, wl["t"], wl["c"], wl["prefix"]
+    g = torch.Generator(device=dev).manual_seed(wl["seed"] * 1000 + rank)
+    frame_out = torch.randn((n * t, c), device=dev, generator=g).to(tdt)
+    global_out = torch.randn((n * t, c), device=dev, generator=g).to(tdt)
+    cache = torch.empty((n * t, 2 * c), device=dev, dtype=torch.float32)
+    reg = torch.empty((n * pre, c), device=dev, dtype=tdt)
+
+    def step():
+        ctx.copy_row_blocks(frame_out, reg, n, t, pre, pre)
+        ctx.copy_row_blocks(reg, frame_out, n, pre, t, pre)
+        ctx.cache_build(frame_out, global_out, out=cache)
+
+    esz = frame_out.element_size()
+    cache_bytes = n * t * 2 * c * (esz + 4)
+    bytes_rank = cache_bytes + 4 * n * pre * c * esz
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        step()
+    ctx.sync()
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(gpu_id_for_smi(local))
+    sampler.start()
+    time.sleep(0.3)
+    ctx.prof_reset()
+    ctx.prof_enable(True)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    ctx.prof_enable(False)
+    clocks = sampler.stop()
+    ctx.sync()
+    ms = max_over_ranks(e0.elapsed_time(e1), world) / args.steps
+    cb_ms, cb_n = ctx.prof_read("cache_build")
+    value = bytes_rank * world / (ms / 1e3) / 1e9
+    peaks_hbm = None
+    mp = ROOT / "MEASURED_PEAKS.json"
+    if mp.exists():
+        peaks_hbm = float(json.loads(mp.read_text()).get("hbm_gbs", 0) or 0) or None
+    peak = peaks_hbm or 6650.0
+    achieved = cache_bytes / (cb_ms / max(cb_n, 1) / 1e3) / 1e9
+    fh, gh = frame_out.cpu().pin_memory(), global_out.cpu().pin_memory()
+    ch = torch.empty(cache.shape, dtype=cache.dtype).pin_memory()
+
+    def e2e_step():
+        ctx.upload(frame_out, fh)
+        ctx.upload(global_out, gh)
+        step()
+        ctx.download(ch, cache)
+
+    e2e_step()
+    torch.cuda.synchronize(dev)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world) / args.steps
+    result = None
+    if rank == 0:
+        result = {
+            "metric": "trunk glue GB/s (f32 head-input cache build + register gather/scatter) at 100 frames",
+            "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": wl["dtype"], "data": f"synthetic N(0,1), seed {wl['seed']}",
+            "config": {"workload": wl["name"], "frames": wl["frames"], "t": t, "c": c,
+                       "parallelism": f"frame-sharded x{world}",
+                       "l2": "each buffer larger than L2 (cache 1.1 GB); no flush needed"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": None,
+                         "peak_source": "measured copy bandwidth (MEASURED_PEAKS.json)" if peaks_hbm else "fallback",
+                         "kernel": "cache_build_kernel", "kernel_ms_per_launch": round(cb_ms / max(cb_n, 1), 3),
+                         "launches": cb_n},
+            "cpu_baseline": None,
+            "e2e": {"value": round(bytes_rank * world / (e2e_ms / 1e3) / 1e9, 1), "unit": "GB/s",
+                    "h2d_bytes_per_step": 2 * frame_out.numel() * esz * world,
+                    "d2h_bytes_per_step": cache.numel() * 4 * world, "ms_per_step": round(e2e_ms, 3)},
+            "gpu_launches": 3 * args.steps * world,
+            "clocks": clocks,
+        }
+    ctx.close()
+    return result
+
+
 def cpu_mlp_sample(x, w1, w2, res, ls, threads: int) -> dict:
     """The reference path on the CPU (oracle linear.wesl + gelu.wesl + residual_ls.wesl) on a
     bounded sample of rows (rows are independent)."""
@@ -716,7 +822,11 @@ def main():
         rank = int(os.environ.get("RANK", "0"))
         if rank != 0:
             return 0
-        ref = run_reference_mlp(args, wl) if wl.get("kind") == "mlp" else run_reference(args, wl)
+        if wl.get("kind") == "glue":
+            ref = {"impl": "reference", "unavailable": "trunk glue workload: the reference's copy/concat/cast "
+                   "kernels are WGSL (no Vulkan on this box); no CPU path of its own"}
+        else:
+            ref = run_reference_mlp(args, wl) if wl.get("kind") == "mlp" else run_reference(args, wl)
         print(json.dumps(ref), file=out, flush=True)
         return 0
 
@@ -724,7 +834,9 @@ def main():
     if world != args.gpus:
         log(f"note: --gpus {args.gpus} but WORLD_SIZE {world}; using {world}")
     try:
-        res = run_mlp(args, wl, rank, world, local) if wl.get("kind") == "mlp" else run_ours(args, wl, rank, world, local)
+        kind = wl.get("kind")
+        runner = run_mlp if kind == "mlp" else run_glue if kind == "glue" else run_ours
+        res = runner(args, wl, rank, world, local)
     finally:
         if world > 1:
             import torch.distributed as dist

@@ -68,6 +68,8 @@ SIGNATURES = {
     "hs_attention_block_fused": (_i, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _i, _f32, _vp, _vp, _vp,
                                       _vp, _f32, _vp, _vp, _u32, _u32, _u32]),
     "hs_linear": (_i, [_vp, _vp, _vp, _vp, _vp, _u64, _u32, _u32, _i, _i, _vp, _vp]),
+    "hs_copy_row_blocks": (_i, [_vp, _vp, _vp, _u64, _u64, _u64, _u64, _u32, _i]),
+    "hs_cache_build": (_i, [_vp, _vp, _vp, _vp, _u64, _u32, _u32, _i]),
     "hs_layernorm": (_i, [_vp, _vp, _vp, _vp, _vp, _u64, _u32, _f32, _i]),
     "hs_rope_apply": (_i, [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _u32, _i]),
     "hs_split_heads": (_i, [_vp, _vp, _vp, _u32, _u32, _u32, _u32, _i]),

@@ -537,6 +537,41 @@ hs_status hs_attn_merge(hs_ctx* ctx, const void* x, void* out, uint32_t S, uint3
   return e == cudaSuccess ? HS_OK : cuda_fail(e, "hs_attn_merge");
 }
 
+hs_status hs_copy_row_blocks(hs_ctx* ctx, const void* src, void* dst, uint64_t groups, uint64_t src_stride_rows,
+                             uint64_t dst_stride_rows, uint64_t rows, uint32_t cols, hs_dtype dtype) {
+  const char* name = "hs_copy_row_blocks";
+  if (!ctx) return fail(HS_ERR_INVALID, std::string(name) + ": null context");
+  if (!valid_dtype(dtype)) return fail(HS_ERR_INVALID, std::string(name) + ": unknown dtype");
+  if (groups == 0 || rows == 0 || cols == 0) return HS_OK;
+  if (!src || !dst) return fail(HS_ERR_INVALID, std::string(name) + ": null pointer");
+  const uint64_t row_bytes = static_cast<uint64_t>(cols) * (dtype == HS_F32 ? 4 : 2);
+  if (row_bytes % 16 || !aligned16(src) || !aligned16(dst))
+    return fail(HS_ERR_INVALID, std::string(name) + ": rows must be 16-byte multiples, pointers 16-byte aligned");
+  if ((groups > 1 && (src_stride_rows < rows || dst_stride_rows < rows)))
+    return fail(HS_ERR_INVALID, std::string(name) + ": group strides shorter than the rows copied");
+  DeviceGuard guard(ctx->device);
+  ProfScope prof(ctx, ctx_stream(ctx), "copy_rows");
+  cudaError_t e = launch_copy_row_blocks(ctx_stream(ctx), src, dst, groups, src_stride_rows, dst_stride_rows, rows,
+                                         row_bytes);
+  return e == cudaSuccess ? HS_OK : cuda_fail(e, name);
+}
+
+hs_status hs_cache_build(hs_ctx* ctx, const void* frame_out, const void* global_out, float* out, uint64_t rows,
+                         uint32_t cols_frame, uint32_t cols_global, hs_dtype dtype) {
+  const char* name = "hs_cache_build";
+  if (!ctx) return fail(HS_ERR_INVALID, std::string(name) + ": null context");
+  if (!valid_dtype(dtype)) return fail(HS_ERR_INVALID, std::string(name) + ": unknown dtype");
+  if (rows == 0) return HS_OK;
+  if (!frame_out || !global_out || !out) return fail(HS_ERR_INVALID, std::string(name) + ": null pointer");
+  if (cols_frame % 8 || cols_global % 8 || !aligned16(frame_out) || !aligned16(global_out) || !aligned16(out))
+    return fail(HS_ERR_INVALID, std::string(name) + ": widths must be multiples of 8, pointers 16-byte aligned");
+  DeviceGuard guard(ctx->device);
+  ProfScope prof(ctx, ctx_stream(ctx), "cache_build");
+  cudaError_t e = launch_cache_build(ctx_stream(ctx), frame_out, global_out, out, static_cast<int>(dtype), rows,
+                                     cols_frame, cols_global);
+  return e == cudaSuccess ? HS_OK : cuda_fail(e, name);
+}
+
 hs_status hs_rope_periods(float* out16) {
   if (!out16) return fail(HS_ERR_INVALID, "hs_rope_periods: null out");
   for (int i = 0; i < 16; ++i) out16[i] = powf(100.0f, 2.0f * static_cast<float>(i) / 32.0f);

@@ -90,6 +90,15 @@ cudaError_t launch_attention_sm100(cudaStream_t stream, int elem, const AttnIO& 
                                    uint64_t timeout_ns, std::string* err);
 
 // Row prep for K (and for casts): out = RoPE(LN(x)) in `out_code` storage.
+// Trunk glue (ops.cu): strided row-block copies (register gather/scatter,
+// copy_rows) and the f32 head-input cache row build.  Rows are 16-byte
+// multiples; pointers 16-byte aligned.
+cudaError_t launch_copy_row_blocks(cudaStream_t stream, const void* src, void* dst, uint64_t groups,
+                                   uint64_t src_stride_rows, uint64_t dst_stride_rows, uint64_t rows,
+                                   uint64_t row_bytes);
+cudaError_t launch_cache_build(cudaStream_t stream, const void* a, const void* b, float* out, int code,
+                               uint64_t rows, uint32_t ca, uint32_t cb);
+
 // Epilogues of the block's linears (gemm_sm100.cu).
 enum LinearEpilogue : int { kEpiNone = 0, kEpiGelu = 1, kEpiResidual = 2 };
 

@@ -362,6 +362,47 @@ cudaError_t prep_dispatch_out(cudaStream_t stream, const PrepJobs& jobs, int n_j
   return cudaGetLastError();
 }
 
+// Row blocks: for g < groups, rows [g*src_stride, +rows) of src go to rows
+// [g*dst_stride, +rows) of dst (the trunk's register gather and scatter,
+// trunk.rs:109-122, and copy_rows).  16-byte granules; a block of threads
+// per (group, granule range).
+__global__ void __launch_bounds__(256) copy_row_blocks_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst,
+                                                              uint64_t groups, uint64_t src_stride_g,
+                                                              uint64_t dst_stride_g, uint64_t granules_per_group) {
+  const uint64_t total = groups * granules_per_group;
+  for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+    const uint64_t g = i / granules_per_group, k = i - g * granules_per_group;
+    dst[g * dst_stride_g + k] = __ldg(src + g * src_stride_g + k);
+  }
+}
+
+// Head-input cache row (Cache::build, cache.rs:25-52): out[r] = [f32(a[r]) | f32(b[r])],
+// the concat_channels + cast_to_f32 of the frame- and global-block outputs.
+template <typename T>
+__global__ void __launch_bounds__(256) cache_build_kernel(const T* __restrict__ a, const T* __restrict__ b,
+                                                          float* __restrict__ out, uint64_t rows, uint32_t ca,
+                                                          uint32_t cb) {
+  const uint32_t ga = ca / 8, gb = cb / 8;  // 8-element granules per row
+  const uint64_t total = rows * (ga + gb);
+  for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+    const uint64_t r = i / (ga + gb);
+    const uint32_t k = static_cast<uint32_t>(i - r * (ga + gb));
+    const T* src = k < ga ? a + r * ca + 8ull * k : b + r * cb + 8ull * (k - ga);
+    float v[8];
+    load8(src, v);
+    float4* dst = reinterpret_cast<float4*>(out + r * (ca + cb) + 8ull * k);
+    dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+    dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+  }
+}
+
+unsigned grid_for(uint64_t work) {
+  const uint64_t blocks = (work + 255) / 256;
+  return static_cast<unsigned>(blocks < 148ull * 16 ? (blocks ? blocks : 1) : 148ull * 16);
+}
+
 template <template <typename> class F, typename... A>
 cudaError_t by_code(int code, A... args) {
   switch (code) {
@@ -454,6 +495,39 @@ cudaError_t launch_attn_merge(cudaStream_t stream, const void* x, void* out, int
                               uint32_t t, uint32_t d) {
   if (static_cast<uint64_t>(s) * h * t * d == 0) return cudaSuccess;
   return by_code<PermuteRun>(code, stream, x, out, s, h, t, d, 1);
+}
+
+cudaError_t launch_copy_row_blocks(cudaStream_t stream, const void* src, void* dst, uint64_t groups,
+                                   uint64_t src_stride_rows, uint64_t dst_stride_rows, uint64_t rows,
+                                   uint64_t row_bytes) {
+  if (groups == 0 || rows == 0 || row_bytes == 0) return cudaSuccess;
+  const uint64_t gran = row_bytes / 16;
+  copy_row_blocks_kernel<<<grid_for(groups * rows * gran), 256, 0, stream>>>(
+      static_cast<const uint4*>(src), static_cast<uint4*>(dst), groups, src_stride_rows * gran,
+      dst_stride_rows * gran, rows * gran);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_cache_build(cudaStream_t stream, const void* a, const void* b, float* out, int code,
+                               uint64_t rows, uint32_t ca, uint32_t cb) {
+  if (rows == 0) return cudaSuccess;
+  const unsigned grid = grid_for(rows * (ca + cb) / 8);
+  switch (code) {
+    case kBF16:
+      cache_build_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(a),
+                                                                  static_cast<const __nv_bfloat16*>(b), out, rows,
+                                                                  ca, cb);
+      break;
+    case kF16:
+      cache_build_kernel<__half><<<grid, 256, 0, stream>>>(static_cast<const __half*>(a),
+                                                           static_cast<const __half*>(b), out, rows, ca, cb);
+      break;
+    default:
+      cache_build_kernel<float><<<grid, 256, 0, stream>>>(static_cast<const float*>(a),
+                                                          static_cast<const float*>(b), out, rows, ca, cb);
+      break;
+  }
+  return cudaGetLastError();
 }
 
 }  // namespace hs

@@ -210,6 +210,48 @@ class GpuContext:
                                 _ptr(residual), _ptr(gamma)))
         return out
 
+    def copy_row_blocks(self, src: torch.Tensor, dst: torch.Tensor, groups: int, src_stride: int, dst_stride: int,
+                        rows: int) -> torch.Tensor:
+        """Rows [g*src_stride, +rows) of src -> rows [g*dst_stride, +rows) of dst for g < groups
+        (trunk.rs:109-122's register gather/scatter; groups=1 is copy_rows)."""
+        cols = src.shape[-1]
+        assert dst.shape[-1] == cols and dst.dtype == src.dtype
+        assert (groups - 1) * src_stride + rows <= src.numel() // cols, "src rows"
+        assert (groups - 1) * dst_stride + rows <= dst.numel() // cols, "dst rows"
+        self._check_tensor(src, "src")
+        self._check_tensor(dst, "dst")
+        self._bind_stream()
+        check(self._L.hs_copy_row_blocks(self._h, _ptr(src), _ptr(dst), groups, src_stride, dst_stride, rows, cols,
+                                         _code(src)))
+        return dst
+
+    def gather_prefix(self, x: torch.Tensor, n: int, t: int, prefix: int) -> torch.Tensor:
+        """(N*T, C) -> (N*prefix, C): the prefix tokens of every frame (trunk.rs:109-113)."""
+        out = torch.empty((n * prefix, x.shape[-1]), dtype=x.dtype, device=x.device)
+        return self.copy_row_blocks(x, out, n, t, prefix, prefix)
+
+    def scatter_prefix(self, reg: torch.Tensor, x: torch.Tensor, n: int, t: int, prefix: int) -> torch.Tensor:
+        """Writes (N*prefix, C) back over the prefix rows of every frame of x (trunk.rs:119-121)."""
+        return self.copy_row_blocks(reg, x, n, prefix, t, prefix)
+
+    def cache_build(self, frame_out: torch.Tensor, global_out: torch.Tensor,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+        """(rows, C1) and (rows, C2) -> (rows, C1 + C2) f32 (cache.rs:25-52); writes into out when given."""
+        assert frame_out.dtype == global_out.dtype
+        c1, c2 = frame_out.shape[-1], global_out.shape[-1]
+        rows = frame_out.numel() // c1
+        assert global_out.numel() // c2 == rows, "row mismatch"
+        self._check_tensor(frame_out, "frame_out")
+        self._check_tensor(global_out, "global_out")
+        if out is None:
+            out = torch.empty((rows, c1 + c2), dtype=torch.float32, device=frame_out.device)
+        assert out.dtype == torch.float32 and out.numel() == rows * (c1 + c2), "cache shape"
+        self._check_tensor(out, "out")
+        self._bind_stream()
+        check(self._L.hs_cache_build(self._h, _ptr(frame_out), _ptr(global_out), _ptr(out), rows, c1, c2,
+                                     _code(frame_out)))
+        return out
+
     def layernorm(self, x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:
         """Row LayerNorm over the last dim, f32 statistics (ops.rs:130-153; the reference fixes eps 1e-5)."""
         dim = x.shape[-1]

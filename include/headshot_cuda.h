@@ -243,6 +243,22 @@ HS_API hs_status hs_ring_sync(hs_ring* ring, uint32_t timeout_ms);
 
 /* ------------------------------------------------------ host helpers --- */
 
+/* Trunk glue (src/model/trunk.rs:78-84 and 105-122, GpuContext::copy_rows):
+ * for g < groups, rows [g*src_stride_rows, +rows) of src (row width `cols`
+ * elements of dtype) are copied to rows [g*dst_stride_rows, +rows) of dst.
+ * The register gather is (groups = N, src stride T, dst stride 17, rows 17);
+ * the scatter back swaps the strides; groups = 1 is copy_rows.  Rows must
+ * be 16-byte multiples and pointers 16-byte aligned. */
+HS_API hs_status hs_copy_row_blocks(hs_ctx* ctx, const void* src, void* dst, uint64_t groups,
+                                    uint64_t src_stride_rows, uint64_t dst_stride_rows, uint64_t rows,
+                                    uint32_t cols, hs_dtype dtype);
+
+/* Head-input cache (src/model/cache.rs:25-52: concat_channels + cast_to_f32):
+ * out (rows, cols_frame + cols_global) f32 = [frame_out row | global_out row]
+ * for rows of dtype.  One buffer (no 2 GiB chunking on this device). */
+HS_API hs_status hs_cache_build(hs_ctx* ctx, const void* frame_out, const void* global_out, float* out,
+                                uint64_t rows, uint32_t cols_frame, uint32_t cols_global, hs_dtype dtype);
+
 /* Replaces rope::periods (src/engine/rope.rs:8-10): 100^(2i/32), i < 16. */
 HS_API hs_status hs_rope_periods(float* out16);
 

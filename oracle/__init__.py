@@ -233,6 +233,20 @@ def residual_ls(res: np.ndarray, x: np.ndarray, gamma: np.ndarray) -> np.ndarray
     return out
 
 
+def copy_row_blocks(src: np.ndarray, dst: np.ndarray, groups: int, src_stride: int, dst_stride: int,
+                    rows: int) -> np.ndarray:
+    """GpuContext::copy_rows per group (trunk.rs:109-122: register gather/scatter); returns dst."""
+    for g in range(groups):
+        dst[g * dst_stride:g * dst_stride + rows] = src[g * src_stride:g * src_stride + rows]
+    return dst
+
+
+def cache_build(frame_out: np.ndarray, global_out: np.ndarray) -> np.ndarray:
+    """Cache::build (cache.rs:25-52): concat_channels (concat_channels.wesl) then cast to f32
+    (cast_f16_to_f32.wesl); inputs already hold the values of their storage type."""
+    return np.concatenate([frame_out.astype(np.float32), global_out.astype(np.float32)], axis=-1)
+
+
 def compare(ours: np.ndarray, ref: np.ndarray) -> dict:
     """src/parity.rs:35-60: max_abs, mean_abs, cosine, ref_scale in f64."""
     a = np.asarray(ours, np.float64).ravel()
