@@ -86,6 +86,7 @@ __device__ __forceinline__ void store8(T* p, const float (&v)[8]) {
 
 constexpr int kPrepTokens = 32;     // tokens per block (8 threads per 64-wide row)
 constexpr int kPrepSeqPerBlock = 16;  // sequences (s, h) a block sweeps with one staged table slice
+constexpr int kGlueUnroll = 4;      // independent 16-byte loads in flight per thread in the glue kernels
 
 // One thread's 8 elements of a 64-wide row: [4g, 4g+4) and their RoPE
 // partners [32+4g, 36+4g), raw as stored (8 bytes each half for 16-bit, 16
@@ -369,38 +370,70 @@ cudaError_t prep_dispatch_out(cudaStream_t stream, const PrepJobs& jobs, int n_j
 __global__ void __launch_bounds__(256) copy_row_blocks_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst,
                                                               uint64_t groups, uint64_t src_stride_g,
                                                               uint64_t dst_stride_g, uint64_t granules_per_group) {
+  // Grid-stride over 16-byte granules, kGlueUnroll independent loads in flight per thread
+  // before their stores (one load per thread leaves HBM latency uncovered).
   const uint64_t total = groups * granules_per_group;
-  for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
-    const uint64_t g = i / granules_per_group, k = i - g * granules_per_group;
-    dst[g * dst_stride_g + k] = __ldg(src + g * src_stride_g + k);
+  const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
+  for (uint64_t i0 = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i0 < total;
+       i0 += kGlueUnroll * stride) {
+    uint4 v[kGlueUnroll];
+    uint64_t d[kGlueUnroll];
+#pragma unroll
+    for (int u = 0; u < kGlueUnroll; ++u) {
+      const uint64_t i = i0 + u * stride;
+      if (i < total) {
+        const uint64_t g = i / granules_per_group, k = i - g * granules_per_group;
+        v[u] = __ldg(src + g * src_stride_g + k);
+        d[u] = g * dst_stride_g + k;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kGlueUnroll; ++u)
+      if (i0 + u * stride < total) dst[d[u]] = v[u];
   }
 }
 
 // Head-input cache row (Cache::build, cache.rs:25-52): out[r] = [f32(a[r]) | f32(b[r])],
-// the concat_channels + cast_to_f32 of the frame- and global-block outputs.
+// the concat_channels + cast_to_f32 of the frame- and global-block outputs.  The cache is
+// written once and read much later, so its stores stream past L2 (st.global.cs).
 template <typename T>
 __global__ void __launch_bounds__(256) cache_build_kernel(const T* __restrict__ a, const T* __restrict__ b,
                                                           float* __restrict__ out, uint64_t rows, uint32_t ca,
                                                           uint32_t cb) {
   const uint32_t ga = ca / 8, gb = cb / 8;  // 8-element granules per row
   const uint64_t total = rows * (ga + gb);
-  for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
-    const uint64_t r = i / (ga + gb);
-    const uint32_t k = static_cast<uint32_t>(i - r * (ga + gb));
-    const T* src = k < ga ? a + r * ca + 8ull * k : b + r * cb + 8ull * (k - ga);
-    float v[8];
-    load8(src, v);
-    float4* dst = reinterpret_cast<float4*>(out + r * (ca + cb) + 8ull * k);
-    dst[0] = make_float4(v[0], v[1], v[2], v[3]);
-    dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+  const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
+  for (uint64_t i0 = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i0 < total;
+       i0 += kGlueUnroll * stride) {
+    float v[kGlueUnroll][8];
+    float* dst[kGlueUnroll];
+#pragma unroll
+    for (int u = 0; u < kGlueUnroll; ++u) {
+      const uint64_t i = i0 + u * stride;
+      if (i < total) {
+        const uint64_t r = i / (ga + gb);
+        const uint32_t k = static_cast<uint32_t>(i - r * (ga + gb));
+        const T* src = k < ga ? a + r * ca + 8ull * k : b + r * cb + 8ull * (k - ga);
+        load8(src, v[u]);
+        dst[u] = out + r * (ca + cb) + 8ull * k;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kGlueUnroll; ++u) {
+      if (i0 + u * stride < total) {
+        float4* o = reinterpret_cast<float4*>(dst[u]);
+        __stcs(o, make_float4(v[u][0], v[u][1], v[u][2], v[u][3]));
+        __stcs(o + 1, make_float4(v[u][4], v[u][5], v[u][6], v[u][7]));
+      }
+    }
   }
 }
 
+// Grid of the glue kernels: one thread per kGlueUnroll granules, at most 8 resident
+// 256-thread blocks on each of the 148 SMs (the grid-stride loop covers the rest).
 unsigned grid_for(uint64_t work) {
-  const uint64_t blocks = (work + 255) / 256;
-  return static_cast<unsigned>(blocks < 148ull * 16 ? (blocks ? blocks : 1) : 148ull * 16);
+  const uint64_t blocks = (work + 256 * kGlueUnroll - 1) / (256 * kGlueUnroll);
+  return static_cast<unsigned>(blocks < 148ull * 8 ? (blocks ? blocks : 1) : 148ull * 8);
 }
 
 template <template <typename> class F, typename... A>

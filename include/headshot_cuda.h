@@ -243,7 +243,8 @@ HS_API hs_status hs_ring_sync(hs_ring* ring, uint32_t timeout_ms);
 
 /* ------------------------------------------------------ host helpers --- */
 
-/* Trunk glue (src/model/trunk.rs:78-84 and 105-122, GpuContext::copy_rows):
+/* Trunk glue (src/model/trunk.rs:78-84 and 105-122, GpuContext::copy_rows at
+ * src/engine/tensor.rs:148-160):
  * for g < groups, rows [g*src_stride_rows, +rows) of src (row width `cols`
  * elements of dtype) are copied to rows [g*dst_stride_rows, +rows) of dst.
  * The register gather is (groups = N, src stride T, dst stride 17, rows 17);
