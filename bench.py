@@ -56,6 +56,11 @@ WORKLOADS = {
     "trunk_glue": dict(kind="glue", frames=100, t=1374, c=1024, prefix=17, dtype="bf16", seed=6,
                        name="trunk glue at 100 frames x 1374 tokens, C 1024, bf16: f32 head-input cache "
                             "build (concat + cast) and the register gather/scatter"),
+    # the full aggregator forward (DINO 24 layers + 24 frame/global block
+    # pairs + the 4 head-input caches) over 100 frames of 518x518 RGB, bf16, random weights.
+    "aggregator": dict(kind="aggregator", frames=100, size=518, dtype="bf16", seed=4,
+                       name="VGGT-1B aggregator forward, 100 frames 518x518 (patch 14, 37x37, 5 prefix tokens), "
+                            "bf16, random-init N(0,0.02), LayerScale 1e-5"),
     "frame_block": dict(S=200, H=16, frames=1, T_f=1374, dtype="f16", seed=2, prefix=5, grid=(37, 37), eps=1e-6,
                         layout="block",
                         name="batched frame attention on the projection layout (S*T, H*D) in and merged out, "
@@ -673,6 +678,176 @@ def run_glue(args, wl: dict, rank: int, world: int, local: int) -> dict | None:
     return result
 
 
+def run_aggregator(args, wl: dict, rank: int, world: int, local: int) -> dict | None:
+    """Config 5: Aggregator.forward, frames sharded across ranks, global blocks on the ring."""
+    import torch
+
+    from headshot_b200.aggregator import Aggregator, AggregatorConfig
+    from headshot_b200.engine import GpuContext
+    from headshot_b200.session import RingSession, shard_bounds
+
+    tdt = {"bf16": torch.bfloat16, "f16": torch.float16}[wl["dtype"]]
+    cfg = AggregatorConfig()
+    ctx = GpuContext(local)
+    dev = torch.device("cuda", local)
+    n_total, size = wl["frames"], wl["size"]
+    f0, f1 = shard_bounds(n_total, world, rank)
+    agg = Aggregator(cfg, tdt, seed=wl["seed"], device=dev)
+    g = torch.Generator(device=dev).manual_seed(wl["seed"])
+    images_all = torch.rand((n_total, 3, size, size), device=dev, generator=g)
+    images = images_all[f0:f1].contiguous()
+    del images_all
+    ring = RingSession(ctx, rank, world) if world > 1 else None
+
+    def step(imgs=images):
+        return agg.forward(ctx, imgs, ring=ring, n_total=n_total, frame0=f0)
+
+    fl = agg.flops(n_total, size, size)
+    p = (size // cfg.patch) ** 2
+    reg_att = len(cfg.register_layers) * 4 * cfg.heads * (n_total * cfg.trunk_prefix) ** 2 * (cfg.dim // cfg.heads)
+    att_rank = (fl["attention"] - reg_att) * (f1 - f0) / n_total + reg_att  # register blocks run on every rank
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        caches = step()
+    del caches
+    ctx.sync()
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(gpu_id_for_smi(local))
+    sampler.start()
+    time.sleep(0.3)
+    ctx.prof_reset()
+    ctx.prof_enable(True)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        caches = step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    ctx.prof_enable(False)
+    clocks = sampler.stop()
+    ctx.sync()
+    ms = max_over_ranks(e0.elapsed_time(e1), world) / args.steps
+    att_ms, att_n = ctx.prof_read("attention")
+    lin_ms, lin_n = ctx.prof_read("linear")
+    all_ms, all_n = ctx.prof_read("*")
+    value = n_total / (ms / 1e3)
+
+    # end to end: the rank's images up from pinned host memory, its four caches down
+    ih = images.cpu().pin_memory()
+    ch = [torch.empty(c.shape, dtype=c.dtype).pin_memory() for c in caches]
+
+    def e2e_step():
+        ctx.upload(images, ih)
+        out = step()
+        for hbuf, c in zip(ch, out):
+            ctx.download(hbuf, c)
+        return out
+
+    del caches
+    e2e_step()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ctx.sync()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world) / args.steps
+    if ring is not None:
+        ring.sync()
+        ring.close()
+
+    peaks = measured_peaks()
+    att_achieved = att_rank * args.steps / (att_ms / 1e3) / 1e12
+    lin_achieved = fl["gemm"] * (f1 - f0) / n_total * args.steps / (lin_ms / 1e3) / 1e12
+    result = None
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            cpu = cpu_aggregator_estimate(cfg, n_total, size, args.cpu_threads or _threads(), wl["dtype"])
+        result = {
+            "metric": "aggregator frames/s (BASELINE config 5: VGGT-1B aggregator forward at 100 frames)",
+            "value": round(value, 3), "unit": "frames/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 2), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": wl["dtype"],
+            "data": f"synthetic images U[0,1], random-init weights N(0,0.02), seed {wl['seed']}",
+            "config": {"workload": wl["name"], "frames": n_total, "image": size, "patch": cfg.patch,
+                       "tokens_per_frame": p + cfg.trunk_prefix, "dino_layers": cfg.dino_layers,
+                       "block_pairs": cfg.trunk_pairs, "register_layers": list(cfg.register_layers),
+                       "cached_layers": list(cfg.cached_layers),
+                       "parallelism": f"frame-sharded x{world}" + (", global blocks ring" if world > 1 else ""),
+                       "tflops_per_step": round(fl["total"] / 1e12, 1),
+                       "tflop_s_whole_step": round(fl["total"] / (ms / 1e3) / 1e12, 1),
+                       "l2": "activations larger than L2 (281 MB per token tensor); no flush needed"},
+            "roofline": {"bound": "tensor", "achieved": round(att_achieved, 1), "peak": peaks["bf16_sustained"],
+                         "unit": "TFLOP/s", "frac": round(att_achieved / peaks["bf16_sustained"], 4),
+                         "traffic": None,
+                         "peak_source": f"{peaks['source']} bf16 sustained (MEASURED_PEAKS.json): kernels inside a "
+                                        f"seconds-long step",
+                         "kernel": "attn_fwd_sm100 (all attention launches of the step)",
+                         "attention_share_of_step": round(att_ms / args.steps / ms, 3),
+                         "linear_tflops": round(lin_achieved, 1),
+                         "linear_share_of_step": round(lin_ms / args.steps / ms, 3)},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(n_total / (e2e_ms / 1e3), 3), "unit": "frames/s",
+                    "h2d_bytes_per_step": images.numel() * 4 * world,
+                    "d2h_bytes_per_step": sum(c.numel() * 4 for c in ch) * world, "ms_per_step": round(e2e_ms, 2)},
+            "gpu_launches": int(all_n) * world,
+            "clocks": clocks,
+        }
+    ctx.close()
+    return result
+
+
+def cpu_aggregator_estimate(cfg, frames: int, size: int, threads: int, dtype: str, seconds: float = 12.0) -> dict:
+    """CPU frames/s of the reference path for config 5, extrapolated from timed oracle samples:
+    a fc1-shaped linear (linear.wesl) for the GEMM rate and query rows of one head of global
+    attention (attention.wesl) for the attention rate, each sized to about seconds/2."""
+    import numpy as np
+
+    import oracle
+    from headshot_b200.aggregator import Aggregator
+
+    rng = np.random.default_rng(5)
+    d, hid = cfg.dim, cfg.mlp_hidden
+    w = oracle.round_to(dtype, (0.02 * rng.standard_normal((hid, d))).astype(np.float32))
+
+    def gemm(rows):
+        x = oracle.round_to(dtype, rng.standard_normal((rows, d)).astype(np.float32))
+        t0 = time.perf_counter()
+        oracle.linear(x, w, None, nthreads=threads)
+        return time.perf_counter() - t0
+
+    probe = max(gemm(8 * threads), 1e-3)
+    rows = int(max(8 * threads, 8 * threads * seconds / 2 / probe))
+    g_dt = gemm(rows)
+    gemm_rate = 2.0 * rows * d * hid / g_dt
+    t = ((size // cfg.patch) ** 2 + cfg.trunk_prefix) * frames
+    q, k, v = (oracle.round_to(dtype, rng.standard_normal((1, 1, t, 64)).astype(np.float32)) for _ in range(3))
+
+    def att(n):
+        t0 = time.perf_counter()
+        oracle.attention_rows(q, k, v, rng.integers(0, t, n), nthreads=threads)
+        return time.perf_counter() - t0
+
+    probe = max(att(threads), 1e-3)
+    n_rows = int(max(threads, threads * seconds / 2 / probe))
+    a_dt = att(n_rows)
+    att_rate = 4.0 * n_rows * t * 64 / a_dt
+    fl = Aggregator.flops(type("A", (), {"cfg": cfg})(), frames, size, size)
+    cpu_s = fl["gemm"] / gemm_rate + fl["attention"] / att_rate
+    return {"value": round(frames / cpu_s, 8), "unit": "frames/s", "cores": threads, "kind": "port",
+            "sample": f"extrapolated: {rows} rows of a 1024->4096 linear ({g_dt:.1f} s, {gemm_rate / 1e9:.1f} GFLOP/s) "
+                      f"and {n_rows} query rows of one head over {t} keys ({a_dt:.1f} s, "
+                      f"{att_rate / 1e9:.1f} GFLOP/s), scaled by the forward's GEMM and attention FLOPs; "
+                      f"LayerNorm, GELU, RoPE and copies left out (favours the CPU)",
+            "cpu_seconds_per_forward": round(cpu_s, 1)}
+
+
 def cpu_mlp_sample(x, w1, w2, res, ls, threads: int) -> dict:
     """The reference path on the CPU (oracle linear.wesl + gelu.wesl + residual_ls.wesl) on a
     bounded sample of rows (rows are independent)."""
@@ -790,6 +965,71 @@ def run_reference_mlp(args, wl: dict) -> dict:
             "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+def run_reference_aggregator(args, wl: dict) -> dict:
+    """Config 5 on the CPU: the oracle's linear and attention rates, extrapolated to one
+    forward (cpu_aggregator_estimate); each step re-measures the two samples."""
+    from headshot_b200.aggregator import AggregatorConfig
+
+    cfg = AggregatorConfig()
+    threads = args.cpu_threads or _threads()
+    for _ in range(args.warmup):
+        cpu_aggregator_estimate(cfg, wl["frames"], wl["size"], threads, wl["dtype"], seconds=2.0)
+    vals = []
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        est = cpu_aggregator_estimate(cfg, wl["frames"], wl["size"], threads, wl["dtype"],
+                                      seconds=args.ref_step_seconds)
+        vals.append(est["value"])
+    dt = time.perf_counter() - t0
+    value = float(sum(vals) / len(vals))
+    return {"impl": "reference", "metric": "aggregator frames/s (BASELINE config 5: VGGT-1B aggregator forward at "
+            "100 frames)", "value": round(value, 8), "unit": "frames/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": f"synthetic, rounded to {wl['dtype']}", "config": {"workload": wl["name"]},
+            "cpu_baseline": {"value": round(value, 8), "unit": "frames/s", "cores": threads, "kind": "port",
+                             "sample": est["sample"]},
+            "e2e": {"value": round(value, 8), "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def run_reference_glue(args, wl: dict) -> dict:
+    """The trunk glue on the CPU (the oracle's numpy restatement of copy_rows,
+    concat_channels and cast_to_f32) over a bounded sample of frames."""
+    import numpy as np
+
+    import oracle
+
+    t, c, pre = wl["t"], wl["c"], wl["prefix"]
+    frames = 10
+    rng = np.random.default_rng(wl["seed"])
+    a = oracle.round_to(wl["dtype"], rng.standard_normal((frames * t, c)).astype(np.float32))
+    b = oracle.round_to(wl["dtype"], rng.standard_normal((frames * t, c)).astype(np.float32))
+    a, b = a.astype(np.float16), b.astype(np.float16)  # 2-byte storage on the host (numpy has no bf16)
+    reg = np.empty((frames * pre, c), a.dtype)
+
+    def step():
+        oracle.copy_row_blocks(a, reg, frames, t, pre, pre)
+        oracle.copy_row_blocks(reg, a, frames, pre, t, pre)
+        oracle.cache_build(a, b)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = time.perf_counter() - t0
+    nbytes = frames * t * 2 * c * (2 + 4) + 4 * frames * pre * c * 2
+    value = nbytes * args.steps / dt / 1e9
+    return {"impl": "reference", "metric": "trunk glue GB/s (f32 head-input cache build + register gather/scatter) "
+            "at 100 frames", "value": round(value, 3), "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": wl["dtype"], "data": "synthetic",
+            "config": {"workload": wl["name"]},
+            "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": 1, "kind": "port",
+                             "sample": f"{frames} frames of the 100 (rows are independent), numpy, one thread"},
+            "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
 def _json_out():
     """The one JSON line goes to the original stdout; everything else written to
     file descriptor 1 during the run (NCCL prints its version banner there) is
@@ -823,8 +1063,9 @@ def main():
         if rank != 0:
             return 0
         if wl.get("kind") == "glue":
-            ref = {"impl": "reference", "unavailable": "trunk glue workload: the reference's copy/concat/cast "
-                   "kernels are WGSL (no Vulkan on this box); no CPU path of its own"}
+            ref = run_reference_glue(args, wl)
+        elif wl.get("kind") == "aggregator":
+            ref = run_reference_aggregator(args, wl)
         else:
             ref = run_reference_mlp(args, wl) if wl.get("kind") == "mlp" else run_reference(args, wl)
         print(json.dumps(ref), file=out, flush=True)
@@ -835,7 +1076,7 @@ def main():
         log(f"note: --gpus {args.gpus} but WORLD_SIZE {world}; using {world}")
     try:
         kind = wl.get("kind")
-        runner = run_mlp if kind == "mlp" else run_glue if kind == "glue" else run_ours
+        runner = {"mlp": run_mlp, "glue": run_glue, "aggregator": run_aggregator}.get(kind, run_ours)
         res = runner(args, wl, rank, world, local)
     finally:
         if world > 1:

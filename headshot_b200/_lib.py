@@ -70,6 +70,7 @@ SIGNATURES = {
     "hs_linear": (_i, [_vp, _vp, _vp, _vp, _vp, _u64, _u32, _u32, _i, _i, _vp, _vp]),
     "hs_copy_row_blocks": (_i, [_vp, _vp, _vp, _u64, _u64, _u64, _u64, _u32, _i]),
     "hs_cache_build": (_i, [_vp, _vp, _vp, _vp, _u64, _u32, _u32, _i]),
+    "hs_im2col_patch": (_i, [_vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _vp, _vp, _i]),
     "hs_layernorm": (_i, [_vp, _vp, _vp, _vp, _vp, _u64, _u32, _f32, _i]),
     "hs_rope_apply": (_i, [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _u32, _i]),
     "hs_split_heads": (_i, [_vp, _vp, _vp, _u32, _u32, _u32, _u32, _i]),

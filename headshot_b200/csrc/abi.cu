@@ -547,12 +547,37 @@ hs_status hs_copy_row_blocks(hs_ctx* ctx, const void* src, void* dst, uint64_t g
   const uint64_t row_bytes = static_cast<uint64_t>(cols) * (dtype == HS_F32 ? 4 : 2);
   if (row_bytes % 16 || !aligned16(src) || !aligned16(dst))
     return fail(HS_ERR_INVALID, std::string(name) + ": rows must be 16-byte multiples, pointers 16-byte aligned");
-  if ((groups > 1 && (src_stride_rows < rows || dst_stride_rows < rows)))
+  if (groups > 1 && ((src_stride_rows != 0 && src_stride_rows < rows) || dst_stride_rows < rows))
     return fail(HS_ERR_INVALID, std::string(name) + ": group strides shorter than the rows copied");
   DeviceGuard guard(ctx->device);
   ProfScope prof(ctx, ctx_stream(ctx), "copy_rows");
   cudaError_t e = launch_copy_row_blocks(ctx_stream(ctx), src, dst, groups, src_stride_rows, dst_stride_rows, rows,
                                          row_bytes);
+  return e == cudaSuccess ? HS_OK : cuda_fail(e, name);
+}
+
+hs_status hs_im2col_patch(hs_ctx* ctx, const float* images, void* out, uint32_t n, uint32_t height, uint32_t width,
+                          uint32_t patch, uint32_t row_stride, const float* mean, const float* std_dev,
+                          hs_dtype dtype) {
+  const char* name = "hs_im2col_patch";
+  if (!ctx) return fail(HS_ERR_INVALID, std::string(name) + ": null context");
+  if (!valid_dtype(dtype)) return fail(HS_ERR_INVALID, std::string(name) + ": unknown dtype");
+  if (patch == 0 || height % patch || width % patch)
+    return fail(HS_ERR_INVALID, std::string(name) + ": image sides must be multiples of the patch size");
+  if (row_stride < 3 * patch * patch)
+    return fail(HS_ERR_INVALID, std::string(name) + ": row_stride < 3 * patch * patch");
+  if (static_cast<uint64_t>(n) * height * width == 0) return HS_OK;
+  if (!images || !out) return fail(HS_ERR_INVALID, std::string(name) + ": null pointer");
+  // ImageNet statistics (headshot-shared model.rs IMAGENET_MEAN / IMAGENET_STD) when not given.
+  const float m[3] = {mean ? mean[0] : 0.485f, mean ? mean[1] : 0.456f, mean ? mean[2] : 0.406f};
+  const float sd[3] = {std_dev ? std_dev[0] : 0.229f, std_dev ? std_dev[1] : 0.224f, std_dev ? std_dev[2] : 0.225f};
+  if (!(sd[0] > 0.f) || !(sd[1] > 0.f) || !(sd[2] > 0.f))
+    return fail(HS_ERR_INVALID, std::string(name) + ": std must be positive");
+  const float inv[3] = {1.0f / sd[0], 1.0f / sd[1], 1.0f / sd[2]};
+  DeviceGuard guard(ctx->device);
+  ProfScope prof(ctx, ctx_stream(ctx), "im2col_patch");
+  cudaError_t e = launch_im2col_patch(ctx_stream(ctx), images, out, static_cast<int>(dtype), n, height, width, patch,
+                                      row_stride, m, inv);
   return e == cudaSuccess ? HS_OK : cuda_fail(e, name);
 }
 

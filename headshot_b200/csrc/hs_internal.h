@@ -96,6 +96,9 @@ cudaError_t launch_attention_sm100(cudaStream_t stream, int elem, const AttnIO& 
 cudaError_t launch_copy_row_blocks(cudaStream_t stream, const void* src, void* dst, uint64_t groups,
                                    uint64_t src_stride_rows, uint64_t dst_stride_rows, uint64_t rows,
                                    uint64_t row_bytes);
+cudaError_t launch_im2col_patch(cudaStream_t stream, const float* images, void* out, int code, uint32_t n,
+                                uint32_t height, uint32_t width, uint32_t patch, uint32_t row_stride,
+                                const float mean[3], const float inv_std[3]);
 cudaError_t launch_cache_build(cudaStream_t stream, const void* a, const void* b, float* out, int code,
                                uint64_t rows, uint32_t ca, uint32_t cb);
 

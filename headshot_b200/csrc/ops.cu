@@ -5,6 +5,7 @@
 //   split_heads  GpuContext::split_heads (src/engine/ops.rs:185-200, shaders/split_heads.wesl)
 //   attn_merge   GpuContext::attn_merge  (src/engine/ops.rs:255-267, shaders/attn_merge.wesl)
 // Storage may be f32, f16 or bf16; all arithmetic is f32.
+#include <algorithm>
 #include <type_traits>
 
 #include "hs_internal.h"
@@ -300,6 +301,55 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const T* __restrict__ x,
   for (uint32_t j = lane; j < dim; j += 32) orow[j] = cvt_to<T>((ld_f(xr + j) - mu) * inv * w[j] + b[j]);
 }
 
+// Model-width rows (dim = 256*C, the blocks' norm1/norm2 and the final
+// norms): one warp per row held in registers, lane l owning the 8-element
+// granules l, l+32, ...; 16-byte loads and stores, the same two-pass
+// statistics (mean, then the centred variance) from the registers.
+template <typename T, int C>
+__global__ void __launch_bounds__(256) layernorm_wide_kernel(const T* __restrict__ x, T* __restrict__ out,
+                                                             const float* __restrict__ w,
+                                                             const float* __restrict__ b, uint64_t rows,
+                                                             float eps) {
+  constexpr uint32_t kDim = 256 * C;
+  const uint64_t row = (static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const T* xr = x + row * kDim;
+  float v[C][8];
+#pragma unroll
+  for (int c = 0; c < C; ++c) load8(xr + 8 * (lane + 32 * c), v[c]);
+  float s = 0.f;
+#pragma unroll
+  for (int c = 0; c < C; ++c)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s += v[c][i];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const float mu = s / static_cast<float>(kDim);
+  float q = 0.f;
+#pragma unroll
+  for (int c = 0; c < C; ++c)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      v[c][i] -= mu;
+      q = fmaf(v[c][i], v[c][i], q);
+    }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+  const float inv = rsqrtf(q / static_cast<float>(kDim) + eps);
+  T* orow = out + row * kDim;
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    const uint32_t j = 8 * (lane + 32 * c);
+    float wv[8], bv[8];
+    load8(w + j, wv);
+    load8(b + j, bv);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[c][i] = v[c][i] * inv * wv[i] + bv[i];
+    store8(orow + j, v[c]);
+  }
+}
+
 // One thread per rotation pair, in place (rope_apply.wesl:36-56).
 template <typename T>
 __global__ void __launch_bounds__(256) rope_apply_kernel(T* __restrict__ x, const float* __restrict__ sin_t,
@@ -429,6 +479,38 @@ __global__ void __launch_bounds__(256) cache_build_kernel(const T* __restrict__ 
   }
 }
 
+// Patch embedding front half (im2col_patch.wesl): images (N, 3, H, W) f32 in
+// [0, 1] -> rows (N*P, row_stride) of T, patch-major (n, py, px), column
+// c*ps*ps + ky*ps + kx = (pixel(c, py*ps + ky, px*ps + kx) - mean[c]) *
+// inv_std[c] (the conv weight's (C_out, 3, ps, ps) order); columns
+// [3*ps*ps, row_stride) are zero so the patch GEMM can take a K padded to a
+// 16-byte multiple (3*14*14 = 588 -> 592).
+template <typename T>
+__global__ void __launch_bounds__(256) im2col_patch_kernel(const float* __restrict__ img, T* __restrict__ out,
+                                                           uint32_t n, uint32_t height, uint32_t width, uint32_t ps,
+                                                           uint32_t row_stride, float3 mean, float3 inv_std) {
+  const uint32_t hp = height / ps, wp = width / ps, kk = ps * ps;
+  const uint64_t total = static_cast<uint64_t>(n) * hp * wp * row_stride;
+  for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+    const uint64_t patch = i / row_stride;
+    const uint32_t col = static_cast<uint32_t>(i - patch * row_stride);
+    float v = 0.f;
+    if (col < 3 * kk) {
+      const uint32_t c = col / kk, ky = (col - c * kk) / ps, kx = col - c * kk - ky * ps;
+      const uint64_t frame = patch / (static_cast<uint64_t>(hp) * wp);
+      const uint32_t pi = static_cast<uint32_t>(patch - frame * hp * wp);
+      const uint32_t py = pi / wp, px = pi - py * wp;
+      const float m = c == 0 ? mean.x : c == 1 ? mean.y : mean.z;
+      const float is = c == 0 ? inv_std.x : c == 1 ? inv_std.y : inv_std.z;
+      const float pix = __ldg(img + ((frame * 3 + c) * height + py * ps + ky) * static_cast<uint64_t>(width) +
+                              px * ps + kx);
+      v = (pix - m) * is;
+    }
+    out[i] = cvt_to<T>(v);
+  }
+}
+
 // Grid of the glue kernels: one thread per kGlueUnroll granules, at most 8 resident
 // 256-thread blocks on each of the 148 SMs (the grid-stride loop covers the rest).
 unsigned grid_for(uint64_t work) {
@@ -447,10 +529,27 @@ cudaError_t by_code(int code, A... args) {
 
 template <typename T>
 struct LayerNormRun {
+  template <int C>
+  static void wide(cudaStream_t st, const void* x, void* out, const float* w, const float* b, uint64_t rows,
+                   float eps) {
+    layernorm_wide_kernel<T, C><<<blocks_for(rows * 32, 256), 256, 0, st>>>(
+        static_cast<const T*>(x), static_cast<T*>(out), w, b, rows, eps);
+  }
   static cudaError_t run(cudaStream_t st, const void* x, void* out, const float* w, const float* b, uint64_t rows,
                          uint32_t dim, float eps) {
-    layernorm_kernel<T><<<blocks_for(rows * 32, 256), 256, 0, st>>>(static_cast<const T*>(x), static_cast<T*>(out), w,
-                                                                     b, rows, dim, eps);
+    const bool vec = dim % 256 == 0 && ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out) |
+                                         reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(b)) & 15) == 0;
+    switch (vec ? dim / 256 : 0) {
+      case 1: wide<1>(st, x, out, w, b, rows, eps); break;
+      case 2: wide<2>(st, x, out, w, b, rows, eps); break;
+      case 3: wide<3>(st, x, out, w, b, rows, eps); break;
+      case 4: wide<4>(st, x, out, w, b, rows, eps); break;
+      case 6: wide<6>(st, x, out, w, b, rows, eps); break;
+      case 8: wide<8>(st, x, out, w, b, rows, eps); break;
+      default:
+        layernorm_kernel<T><<<blocks_for(rows * 32, 256), 256, 0, st>>>(static_cast<const T*>(x),
+                                                                         static_cast<T*>(out), w, b, rows, dim, eps);
+    }
     return cudaGetLastError();
   }
 };
@@ -538,6 +637,31 @@ cudaError_t launch_copy_row_blocks(cudaStream_t stream, const void* src, void* d
   copy_row_blocks_kernel<<<grid_for(groups * rows * gran), 256, 0, stream>>>(
       static_cast<const uint4*>(src), static_cast<uint4*>(dst), groups, src_stride_rows * gran,
       dst_stride_rows * gran, rows * gran);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_im2col_patch(cudaStream_t stream, const float* images, void* out, int code, uint32_t n,
+                                uint32_t height, uint32_t width, uint32_t patch, uint32_t row_stride,
+                                const float mean[3], const float inv_std[3]) {
+  const uint64_t total = static_cast<uint64_t>(n) * (height / patch) * (width / patch) * row_stride;
+  if (total == 0) return cudaSuccess;
+  const float3 m = make_float3(mean[0], mean[1], mean[2]);
+  const float3 is = make_float3(inv_std[0], inv_std[1], inv_std[2]);
+  const unsigned grid = static_cast<unsigned>(std::min<uint64_t>((total + 255) / 256, 148ull * 16));
+  switch (code) {
+    case kBF16:
+      im2col_patch_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(images, static_cast<__nv_bfloat16*>(out), n,
+                                                                   height, width, patch, row_stride, m, is);
+      break;
+    case kF16:
+      im2col_patch_kernel<__half><<<grid, 256, 0, stream>>>(images, static_cast<__half*>(out), n, height, width,
+                                                            patch, row_stride, m, is);
+      break;
+    default:
+      im2col_patch_kernel<float><<<grid, 256, 0, stream>>>(images, static_cast<float*>(out), n, height, width, patch,
+                                                           row_stride, m, is);
+      break;
+  }
   return cudaGetLastError();
 }
 

@@ -215,12 +215,19 @@ hs_status hs_ring_destroy(hs_ring* ring) {
   return HS_OK;
 }
 
-hs_status hs_ring_attention_fused(hs_ring* ring, const void* q, const void* k, const void* v, void* out, uint32_t H,
-                                  uint32_t T_total, uint32_t D, hs_dtype dtype, float scale, const float* q_norm_w,
-                                  const float* q_norm_b, const float* k_norm_w, const float* k_norm_b, float eps,
-                                  const float* rope_sin, const float* rope_cos, uint32_t rope_rows, uint32_t prefix,
-                                  uint32_t tokens_per_frame) {
-  const char* name = "hs_ring_attention_fused";
+}  // extern "C"
+
+namespace {
+
+// The ring attention of one rank.  `block`: q, k, v and out are this rank's
+// (T_r, H*64) projection rows (Block::forward's layout) instead of (H, T_r,
+// 64).  Shards are whole `unit`s of tokens (frames, for a frame-sharded
+// trunk): rank r owns units shard(T_total / unit, R, r).
+hs_status ring_attention(hs_ring* ring, const void* q, const void* k, const void* v, void* out, uint32_t H,
+                         uint32_t T_total, uint32_t D, hs_dtype dtype, float scale, const float* q_norm_w,
+                         const float* q_norm_b, const float* k_norm_w, const float* k_norm_b, float eps,
+                         const float* rope_sin, const float* rope_cos, uint32_t rope_rows, uint32_t prefix,
+                         uint32_t tokens_per_frame, bool block, uint32_t unit, const char* name) {
   if (!ring) return hs::abi_fail(HS_ERR_INVALID, std::string(name) + ": null ring");
   if (ring->aborted) return hs::abi_fail(HS_ERR_NCCL, std::string(name) + ": ring was aborted");
   hs_ctx* ctx = ring->ctx;
@@ -229,10 +236,18 @@ hs_status hs_ring_attention_fused(hs_ring* ring, const void* q, const void* k, c
   if (dtype != HS_F16 && dtype != HS_BF16)
     return hs::abi_fail(HS_ERR_UNSUPPORTED, std::string(name) + ": ring path takes f16/bf16 storage");
   if (D != 64) return hs::abi_fail(HS_ERR_UNSUPPORTED, std::string(name) + ": head_dim must be 64");
-  if (H == 0 || H > 65535 || T_total < static_cast<uint32_t>(R))
-    return hs::abi_fail(HS_ERR_INVALID, std::string(name) + ": need 1 <= H <= 65535 and T_total >= world");
+  if (unit == 0 || T_total % unit != 0)
+    return hs::abi_fail(HS_ERR_INVALID, std::string(name) + ": T_total must be a multiple of shard_unit");
+  if (H == 0 || H > 65535 || T_total / unit < static_cast<uint32_t>(R))
+    return hs::abi_fail(HS_ERR_INVALID, std::string(name) + ": need 1 <= H <= 65535 and one shard unit per rank");
+  // Token range [t0, t0 + len) of rank i's shard.
+  auto shard_of = [&](int i, uint32_t* t0_, uint32_t* len_) {
+    shard(T_total / unit, R, i, t0_, len_);
+    *t0_ *= unit;
+    *len_ *= unit;
+  };
   uint32_t t0, tr;
-  shard(T_total, R, r, &t0, &tr);
+  shard_of(r, &t0, &tr);
   if (!q || !k || !v || !out) return hs::abi_fail(HS_ERR_INVALID, std::string(name) + ": null tensor pointer");
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
     return hs::abi_fail(HS_ERR_INVALID, std::string(name) + ": tensor pointers must be 16-byte aligned");
@@ -251,7 +266,7 @@ hs_status hs_ring_attention_fused(hs_ring* ring, const void* q, const void* k, c
   cudaStream_t cs = ring->comm_stream;
   const int code = static_cast<int>(dtype);
   const size_t row_bytes = 64 * 2;
-  const uint32_t tmax = (T_total + R - 1) / R;
+  const uint32_t tmax = (T_total / unit + R - 1) / R * unit;
   const size_t need_buf = 2ull * H * tmax * row_bytes;
   cudaError_t e;
   if (ring->buf_bytes < need_buf && R > 1) {
@@ -291,9 +306,20 @@ hs_status hs_ring_attention_fused(hs_ring* ring, const void* q, const void* k, c
   kp.ln_b = k_norm_b;
 
   if (R == 1) {  // nothing to exchange: the single-device fused op
+    if (block)
+      return hs_attention_block_fused(ctx, q, k, v, out, 1, T_total, H, D, dtype, scale, q_norm_w, q_norm_b,
+                                      k_norm_w, k_norm_b, eps, rope_sin, rope_cos, rope_rows, prefix,
+                                      tokens_per_frame);
     return hs_attention_fused(ctx, q, k, v, out, 1, H, T_total, D, dtype, scale, q_norm_w, q_norm_b, k_norm_w,
                               k_norm_b, eps, rope_sin, rope_cos, rope_rows, prefix, tokens_per_frame);
   }
+  // Where this rank's q, k, v and out rows live, and the layout of the K and V
+  // halves of a ring block: K' head-major when the prologue writes it, else K
+  // as given; V as given.  Every rank uses the same call, so every block
+  // arriving over the ring has the sender's layout, which is this one.
+  auto given = [&](uint32_t t) {
+    return block ? hs::RowLayout::token_major(H, t, static_cast<uint64_t>(H) * 64) : hs::RowLayout::head_major(H, t);
+  };
 
   // Block 0 = this rank's [K' | V] in buf[0], and this rank's Q'.  The
   // preps also record the largest q' and k' row norms; an all-ranks max of
@@ -307,9 +333,9 @@ hs_status hs_ring_attention_fused(hs_ring* ring, const void* q, const void* k, c
     kp.norm2_max = ring->norm2 + 1;
     qp.norm2_max = ring->norm2;
   }
-  const hs::RowLayout hm = hs::RowLayout::head_major(H, tr);
+  const hs::RowLayout in_rows = given(tr);
   if (bounded) {  // K' into block 0 and Q' into the state buffer, one launch
-    const hs::PrepJob jobs[2] = {{k, hm, b0, kp}, {q, hm, ring->state, qp}};
+    const hs::PrepJob jobs[2] = {{k, in_rows, b0, kp}, {q, in_rows, ring->state, qp}};
     {
       hs::ProfScope prof(ctx, st, "qk_prep");
       e = hs::launch_qk_prep(st, code, code, 1, H, tr, jobs, 2);
@@ -340,13 +366,13 @@ hs_status hs_ring_attention_fused(hs_ring* ring, const void* q, const void* k, c
     int src, send_to, recv_from, load, store;
     hs_ring_plan(r, R, s, &src, &send_to, &recv_from, &load, &store);
     uint32_t src_t0, src_len;
-    shard(T_total, R, src, &src_t0, &src_len);
+    shard_of(src, &src_t0, &src_len);
     uint8_t* cur = static_cast<uint8_t*>(ring->buf[s % 2]);
     uint8_t* nxt = static_cast<uint8_t*>(ring->buf[(s + 1) % 2]);
     if (send_to >= 0) {
       const int nsrc = (src - 1 + R) % R;  // the block the previous rank holds now
       uint32_t n_t0, n_len;
-      shard(T_total, R, nsrc, &n_t0, &n_len);
+      shard_of(nsrc, &n_t0, &n_len);
       if (s == 0) cudaStreamWaitEvent(cs, ring->ev_block0, 0);
       if (s >= 1) cudaStreamWaitEvent(cs, ring->ev_compute[(s - 1) % 2], 0);  // nxt was read by step s-1
       ncclResult_t nr = n.GroupStart();
@@ -365,13 +391,13 @@ hs_status hs_ring_attention_fused(hs_ring* ring, const void* q, const void* k, c
       hs::ProfScope prof(ctx, st, "attention");
       hs::AttnIO io;
       io.q = q_use;
-      io.lq = hs::RowLayout::head_major(H, tr);
+      io.lq = bounded ? hs::RowLayout::head_major(H, tr) : given(tr);
       io.k = cur;
-      io.lk = hs::RowLayout::head_major(H, src_len);
+      io.lk = bounded ? hs::RowLayout::head_major(H, src_len) : given(src_len);
       io.v = cur + static_cast<size_t>(H) * src_len * row_bytes;
-      io.lv = io.lk;
+      io.lv = given(src_len);
       io.out = out;
-      io.lo = io.lq;
+      io.lo = given(tr);
       io.out_code = code;
       e = hs::launch_attention_sm100(st, code, io, 1, H, tr, src_len, scale, state, 0, ctx->d_status, ctx->d_sched,
                                      bounded ? ring->norm2 : nullptr, true, hs::ctx_timeout_ns(ctx), &err);
@@ -382,6 +408,31 @@ hs_status hs_ring_attention_fused(hs_ring* ring, const void* q, const void* k, c
   }
   cudaEventRecord(ring->ev_done, st);
   return HS_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+hs_status hs_ring_attention_fused(hs_ring* ring, const void* q, const void* k, const void* v, void* out, uint32_t H,
+                                  uint32_t T_total, uint32_t D, hs_dtype dtype, float scale, const float* q_norm_w,
+                                  const float* q_norm_b, const float* k_norm_w, const float* k_norm_b, float eps,
+                                  const float* rope_sin, const float* rope_cos, uint32_t rope_rows, uint32_t prefix,
+                                  uint32_t tokens_per_frame) {
+  return ring_attention(ring, q, k, v, out, H, T_total, D, dtype, scale, q_norm_w, q_norm_b, k_norm_w, k_norm_b, eps,
+                        rope_sin, rope_cos, rope_rows, prefix, tokens_per_frame, false, 1,
+                        "hs_ring_attention_fused");
+}
+
+hs_status hs_ring_attention_block_fused(hs_ring* ring, const void* q, const void* k, const void* v, void* out,
+                                        uint32_t H, uint32_t T_total, uint32_t D, hs_dtype dtype, float scale,
+                                        const float* q_norm_w, const float* q_norm_b, const float* k_norm_w,
+                                        const float* k_norm_b, float eps, const float* rope_sin,
+                                        const float* rope_cos, uint32_t rope_rows, uint32_t prefix,
+                                        uint32_t tokens_per_frame, uint32_t shard_unit) {
+  return ring_attention(ring, q, k, v, out, H, T_total, D, dtype, scale, q_norm_w, q_norm_b, k_norm_w, k_norm_b, eps,
+                        rope_sin, rope_cos, rope_rows, prefix, tokens_per_frame, true, shard_unit,
+                        "hs_ring_attention_block_fused");
 }
 
 hs_status hs_ring_sync(hs_ring* ring, uint32_t timeout_ms) {

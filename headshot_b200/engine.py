@@ -252,6 +252,29 @@ class GpuContext:
                                      _code(frame_out)))
         return out
 
+    def im2col_patch(self, images: torch.Tensor, patch: int = 16, dtype: torch.dtype = torch.float32,
+                     row_stride: int | None = None, mean=(0.485, 0.456, 0.406),
+                     std=(0.229, 0.224, 0.225)) -> torch.Tensor:
+        """images (N, 3, H, W) f32 -> normalised patch rows (N*P, row_stride) (ops.rs:271-300);
+        row_stride defaults to 3*patch*patch, wider strides are zero-padded."""
+        assert images.dim() == 4 and images.shape[1] == 3, "images (N,3,H,W)"
+        assert images.dtype == torch.float32, "images are uploaded f32"
+        n, _, height, width = images.shape
+        assert height % patch == 0 and width % patch == 0, "image sides must be multiples of the patch"
+        k = 3 * patch * patch
+        row_stride = k if row_stride is None else row_stride
+        assert row_stride >= k
+        self._check_tensor(images, "images")
+        p = (height // patch) * (width // patch)
+        out = torch.empty((n * p, row_stride), dtype=dtype, device=images.device)
+        m = (ctypes.c_float * 3)(*mean)
+        sd = (ctypes.c_float * 3)(*std)
+        self._bind_stream()
+        check(self._L.hs_im2col_patch(self._h, _ptr(images), _ptr(out), n, height, width, patch, row_stride,
+                                      ctypes.cast(m, ctypes.c_void_p), ctypes.cast(sd, ctypes.c_void_p),
+                                      _DTYPES[dtype]))
+        return out
+
     def layernorm(self, x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:
         """Row LayerNorm over the last dim, f32 statistics (ops.rs:130-153; the reference fixes eps 1e-5)."""
         dim = x.shape[-1]

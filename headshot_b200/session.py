@@ -34,6 +34,8 @@ RING_SIGNATURES = {
     "hs_ring_destroy": (_i, [_vp]),
     "hs_ring_attention_fused": (_i, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _i, _f32, _vp, _vp, _vp, _vp, _f32,
                                      _vp, _vp, _u32, _u32, _u32]),
+    "hs_ring_attention_block_fused": (_i, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _i, _f32, _vp, _vp, _vp, _vp,
+                                           _f32, _vp, _vp, _u32, _u32, _u32, _u32]),
     "hs_ring_sync": (_i, [_vp, _u32]),
 }
 
@@ -151,6 +153,36 @@ class RingSession:
             self._h, _ptr(q), _ptr(k), _ptr(v), _ptr(out), h, T_total, 64, _code(q),
             0.0 if scale is None else float(scale), *[_ptr(x) for x in n_args], float(eps), _ptr(r_sin), _ptr(r_cos),
             rows, prefix, tpf))
+        return out
+
+    def unit_shard(self, t_total: int, unit: int) -> tuple[int, int]:
+        """Token range of this rank when shards are whole `unit`s of tokens (whole frames)."""
+        assert t_total % unit == 0, "t_total must be a multiple of the shard unit"
+        u0, u1 = shard_bounds(t_total // unit, self.world, self.rank)
+        return u0 * unit, u1 * unit
+
+    def attention_block(self, q, k, v, out, T_total: int, heads: int, shard_unit: int = 1, qk_norm=None, rope=None,
+                        scale: float | None = None, check_peers: bool = False):
+        """Ring global attention on Block::forward's layout: q, k, v are this rank's (T_r, H*64) q/k/v
+        linear outputs, out its (T_r, H*64) merged output; shards are whole `shard_unit`s of tokens
+        (hs_ring_attention_block_fused)."""
+        import torch
+
+        from .engine import _code, _ptr
+
+        if check_peers:
+            preflight(self.group)
+        t0, t1 = self.unit_shard(T_total, shard_unit)
+        assert q.shape[-1] == heads * 64 and q.numel() == (t1 - t0) * heads * 64, \
+            f"rank {self.rank} owns {t1 - t0} tokens of (T, {heads * 64})"
+        for x in (q, k, v, out):
+            assert x.shape == q.shape and x.dtype == q.dtype and x.is_contiguous()
+        pro = self.ctx._prologue_args(64, T_total, qk_norm, rope)
+        check(self._L.hs_ctx_set_stream(self.ctx.handle,
+                                        ctypes.c_void_p(torch.cuda.current_stream(self.ctx.device).cuda_stream)))
+        check(self._L.hs_ring_attention_block_fused(
+            self._h, _ptr(q), _ptr(k), _ptr(v), _ptr(out), heads, T_total, 64, _code(q),
+            0.0 if scale is None else float(scale), *pro, shard_unit))
         return out
 
     def sync(self, timeout_ms: int = 120_000) -> None:

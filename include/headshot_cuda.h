@@ -236,6 +236,20 @@ HS_API hs_status hs_ring_attention_fused(hs_ring* ring, const void* q, const voi
                                          const float* k_norm_b, float eps, const float* rope_sin,
                                          const float* rope_cos, uint32_t rope_rows, uint32_t prefix,
                                          uint32_t tokens_per_frame);
+/* hs_ring_attention_fused on Block::forward's layout (block.rs:130-149),
+ * for a trunk whose tokens are sharded across ranks by whole frames: q, k, v
+ * are this rank's (T_r, H*D) rows of the q/k/v linears and out its (T_r,
+ * H*D) merged attention output (the proj linear's input).  Rank r owns the
+ * tokens of units shard(T_total / shard_unit, world, r) (hs_ring_shard's
+ * rule over units; shard_unit = tokens per frame keeps frames whole);
+ * T_total must be a multiple of shard_unit.  Every rank passes the same
+ * T_total, shard_unit and prologue. */
+HS_API hs_status hs_ring_attention_block_fused(hs_ring* ring, const void* q, const void* k, const void* v, void* out,
+                                               uint32_t H, uint32_t T_total, uint32_t D, hs_dtype dtype, float scale,
+                                               const float* q_norm_w, const float* q_norm_b, const float* k_norm_w,
+                                               const float* k_norm_b, float eps, const float* rope_sin,
+                                               const float* rope_cos, uint32_t rope_rows, uint32_t prefix,
+                                               uint32_t tokens_per_frame, uint32_t shard_unit);
 /* Waits for the ring's work with a host-side watchdog: on an NCCL async
  * error or after timeout_ms the communicator is aborted and the ring
  * becomes unusable (HS_ERR_NCCL / HS_ERR_TIMEOUT). */
@@ -249,10 +263,24 @@ HS_API hs_status hs_ring_sync(hs_ring* ring, uint32_t timeout_ms);
  * elements of dtype) are copied to rows [g*dst_stride_rows, +rows) of dst.
  * The register gather is (groups = N, src stride T, dst stride 17, rows 17);
  * the scatter back swaps the strides; groups = 1 is copy_rows.  Rows must
- * be 16-byte multiples and pointers 16-byte aligned. */
+ * be 16-byte multiples and pointers 16-byte aligned.  src_stride_rows = 0
+ * copies the same source rows into every group (the per-frame camera and
+ * register tokens of trunk.rs:78-84, the cls/storage tokens of dino.rs). */
 HS_API hs_status hs_copy_row_blocks(hs_ctx* ctx, const void* src, void* dst, uint64_t groups,
                                     uint64_t src_stride_rows, uint64_t dst_stride_rows, uint64_t rows,
                                     uint32_t cols, hs_dtype dtype);
+
+/* Patch embedding front half (GpuContext::im2col_patch, ops.rs:271-300 ->
+ * im2col_patch.wesl): images (n, 3, height, width) f32 in [0, 1] -> out
+ * (n * (height/patch) * (width/patch), row_stride) of dtype, row = one patch
+ * (frame-major, then patch row, patch column), column c*patch*patch +
+ * ky*patch + kx = (pixel - mean[c]) / std[c]; columns from 3*patch*patch to
+ * row_stride are written as zero (a K padded for the patch GEMM).  mean and
+ * std are host arrays of 3, or NULL for the ImageNet statistics.  The
+ * reference fixes patch = 16 and row_stride = 768. */
+HS_API hs_status hs_im2col_patch(hs_ctx* ctx, const float* images, void* out, uint32_t n, uint32_t height,
+                                 uint32_t width, uint32_t patch, uint32_t row_stride, const float* mean,
+                                 const float* std_dev, hs_dtype dtype);
 
 /* Head-input cache (src/model/cache.rs:25-52: concat_channels + cast_to_f32):
  * out (rows, cols_frame + cols_global) f32 = [frame_out row | global_out row]
