@@ -14,7 +14,11 @@ import numpy as np
 sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
 
 
-def run(rank: int, world: int, port: int, outdir: str, T: int, H: int, dtype: str, seed: int, fused: bool) -> None:
+def run(rank: int, world: int, port: int, outdir: str, T: int, H: int, dtype: str, seed: int, fused: bool,
+        unit: int = 0) -> None:
+    """unit = 0: head-major (1, H, T_r, 64) shards of hs_shard's token rule (attention_fused);
+    unit > 0: the (T_r, H*64) projection layout in shards of whole `unit`-token frames
+    (attention_block)."""
     import torch
     import torch.distributed as dist
 
@@ -34,9 +38,18 @@ def run(rank: int, world: int, port: int, outdir: str, T: int, H: int, dtype: st
         tdt = {"bf16": torch.bfloat16, "f16": torch.float16}[dtype]
         rng = np.random.default_rng(seed)
         q, k, v = (oracle.round_to(dtype, rng.standard_normal((1, H, T, 64), np.float32)) for _ in range(3))
-        t0, t1 = sess.shard(T)
-        loc = lambda a: torch.from_numpy(np.ascontiguousarray(a[:, :, t0:t1])).to(dev).to(tdt)  # noqa: E731
-        out = torch.empty((1, H, t1 - t0, 64), dtype=tdt, device=dev)
+        if unit:
+            t0, t1 = sess.unit_shard(T, unit)
+
+            def loc(a):  # (1, H, T, 64) -> this rank's (T_r, H*64) rows
+                rows = oracle.attn_merge(a)[t0:t1]
+                return torch.from_numpy(np.ascontiguousarray(rows)).to(dev).to(tdt)
+
+            out = torch.empty((t1 - t0, H * 64), dtype=tdt, device=dev)
+        else:
+            t0, t1 = sess.shard(T)
+            loc = lambda a: torch.from_numpy(np.ascontiguousarray(a[:, :, t0:t1])).to(dev).to(tdt)  # noqa: E731
+            out = torch.empty((1, H, t1 - t0, 64), dtype=tdt, device=dev)
         norm = rope = None
         if fused:
             w = torch.ones(64, device=dev)
@@ -45,7 +58,12 @@ def run(rank: int, world: int, port: int, outdir: str, T: int, H: int, dtype: st
             sin, cos = oracle.rope_tables(37, 37)
             rope = Rope(torch.from_numpy(sin).to(dev), torch.from_numpy(cos).to(dev), 5, 1374)
         for _ in range(2):  # the second call reuses the ring's buffers and state
-            sess.attention_fused(loc(q), loc(k), loc(v), out, T_total=T, qk_norm=norm, rope=rope, check_peers=True)
+            if unit:
+                sess.attention_block(loc(q), loc(k), loc(v), out, T_total=T, heads=H, shard_unit=unit,
+                                     qk_norm=norm, rope=rope, check_peers=True)
+            else:
+                sess.attention_fused(loc(q), loc(k), loc(v), out, T_total=T, qk_norm=norm, rope=rope,
+                                     check_peers=True)
             sess.sync(60_000)
         np.save(Path(outdir) / f"out_{rank}.npy", out.float().cpu().numpy())
         sess.close()
@@ -56,4 +74,5 @@ def run(rank: int, world: int, port: int, outdir: str, T: int, H: int, dtype: st
 
 if __name__ == "__main__":
     a = sys.argv[1:]
-    run(int(a[0]), int(a[1]), int(a[2]), a[3], int(a[4]), int(a[5]), a[6], int(a[7]), a[8] == "1")
+    run(int(a[0]), int(a[1]), int(a[2]), a[3], int(a[4]), int(a[5]), a[6], int(a[7]), a[8] == "1",
+        int(a[9]) if len(a) > 9 else 0)

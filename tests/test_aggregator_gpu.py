@@ -107,12 +107,30 @@ SMALL = {
 }
 
 
+def small_images(n: int, h: int, w: int) -> np.ndarray:
+    return np.random.default_rng(11).random((n, 3, h, w), dtype=np.float32)
+
+
+def _oracle_caches(agg: Aggregator, images: np.ndarray, taps: dict | None = None) -> list:
+    cfg = agg.cfg
+    n, _, h, w = images.shape
+    dino_w, trunk_w = _weights_np(agg)
+    tokens = omodel.dino_forward(images, dino_w, cfg, "bf16", taps)
+    return omodel.trunk_forward(tokens, trunk_w, cfg, n, h // cfg.patch, w // cfg.patch, "bf16", taps)
+
+
+def _close(ours: np.ndarray, ref: np.ndarray, what) -> None:
+    # bf16 storage after every op and a few layers deep: cosine >= 0.999 and max |diff|
+    # within 5 % of the tensor's scale (one ulp of bf16 is 0.4-0.8 %).
+    m = oracle.compare(ours, ref)
+    assert m["cosine"] >= 0.999 and m["max_abs"] <= 0.05 * max(1.0, m["ref_scale"]), (what, m)
+
+
 @pytest.mark.parametrize("name", sorted(SMALL))
 def test_aggregator_matches_oracle(gpu_ctx, name):
     cfg, (h, w), n = SMALL[name]
     agg = Aggregator(cfg, torch.bfloat16, seed=7, device=0)
-    rng = np.random.default_rng(11)
-    images = rng.random((n, 3, h, w), dtype=np.float32)
+    images = small_images(n, h, w)
     taps = {}
 
     def tap(key, t):
@@ -120,20 +138,46 @@ def test_aggregator_matches_oracle(gpu_ctx, name):
 
     caches = agg.forward(gpu_ctx, torch.from_numpy(images).cuda(), tap=tap)
     gpu_ctx.sync()
-    dino_w, trunk_w = _weights_np(agg)
     ref_taps = {}
-    tokens = omodel.dino_forward(images, dino_w, cfg, "bf16", ref_taps)
-    ref_caches = omodel.trunk_forward(tokens, trunk_w, cfg, n, h // cfg.patch, w // cfg.patch, "bf16", ref_taps)
+    ref_caches = _oracle_caches(agg, images, ref_taps)
     assert len(caches) == len(ref_caches) == len(cfg.cached_layers)
-    # bf16 storage after every op and a few layers deep: cosine >= 0.999 and max |diff|
-    # within 5 % of the tensor's scale (one ulp of bf16 is 0.4-0.8 %).
     for key in ["dino.tokens"] + [k for k in ref_taps if k.startswith("trunk.")]:
-        m = oracle.compare(taps[key], ref_taps[key])
-        assert m["cosine"] >= 0.999 and m["max_abs"] <= 0.05 * max(1.0, m["ref_scale"]), (key, m)
+        _close(taps[key], ref_taps[key], key)
     for ours, ref in zip(caches, ref_caches):
         assert ours.dtype == torch.float32 and tuple(ours.shape) == ref.shape
-        m = oracle.compare(host(ours), ref)
-        assert m["cosine"] >= 0.999 and m["max_abs"] <= 0.05 * max(1.0, m["ref_scale"]), m
+        _close(host(ours), ref, "cache")
+
+
+@pytest.mark.parametrize("name", sorted(SMALL))
+def test_aggregator_frame_sharded_ring(tmp_path, name):
+    """Two ranks (one process per GPU): frames sharded unevenly (2 + 1 or 1 + 1), global
+    blocks on the ring in whole-frame shards, register layers on the all-gathered prefix
+    rows; the rows of both ranks' caches must match the oracle's single-device forward."""
+    import os
+    import socket
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    world = 2
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    here = Path(__file__).resolve().parent
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    procs = [subprocess.Popen([sys.executable, str(here / "_aggregator_worker.py"), str(r), str(world), str(port),
+                               str(tmp_path), name], env=env) for r in range(world)]
+    rcs = [p.wait(timeout=600) for p in procs]
+    assert rcs == [0] * world, f"worker exit codes {rcs}"
+    cfg, (h, w), n = SMALL[name]
+    agg = Aggregator(cfg, torch.bfloat16, seed=7, device=0)
+    ref_caches = _oracle_caches(agg, small_images(n, h, w))
+    for i, ref in enumerate(ref_caches):
+        ours = np.concatenate([np.load(tmp_path / f"cache{i}_{r}.npy") for r in range(world)])
+        assert ours.shape == ref.shape
+        _close(ours, ref, f"cache {i}")
 
 
 def test_aggregator_cancel(gpu_ctx):

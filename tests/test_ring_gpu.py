@@ -33,19 +33,28 @@ def _gpus() -> int:
     return torch.cuda.device_count() if torch.cuda.is_available() else 0
 
 
-@pytest.mark.parametrize("world,T,fused,dtype", [(2, 2748, True, "bf16"), (2, 2748, True, "f16"), (2, 1001, False, "f16")])
-def test_ring_matches_oracle(tmp_path, world, T, fused, dtype):
+# unit 0: head-major shards of the token rule; unit > 0: projection-layout rows in shards of
+# whole frames (the frame-sharded trunk's global blocks), uneven when frames % world != 0.
+@pytest.mark.parametrize("world,T,fused,dtype,unit", [(2, 2748, True, "bf16", 0), (2, 2748, True, "f16", 0),
+                                                      (2, 1001, False, "f16", 0), (2, 4122, True, "bf16", 1374),
+                                                      (2, 1001, False, "bf16", 143)])
+def test_ring_matches_oracle(tmp_path, world, T, fused, dtype, unit):
     if _gpus() < world:
         pytest.skip(f"needs {world} GPUs")
     H, seed = 2, 17
     port = _free_port()
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     procs = [subprocess.Popen([sys.executable, str(HERE / "_ring_worker.py"), str(r), str(world), str(port),
-                               str(tmp_path), str(T), str(H), dtype, str(seed), "1" if fused else "0"], env=env)
+                               str(tmp_path), str(T), str(H), dtype, str(seed), "1" if fused else "0", str(unit)],
+                              env=env)
              for r in range(world)]
     rcs = [p.wait(timeout=600) for p in procs]
     assert rcs == [0] * world, f"worker exit codes {rcs}"
-    out = np.concatenate([np.load(tmp_path / f"out_{r}.npy") for r in range(world)], axis=2)
+    parts = [np.load(tmp_path / f"out_{r}.npy") for r in range(world)]
+    if unit:
+        out = oracle.split_heads(np.concatenate(parts, axis=0), 1, T, H, 64)
+    else:
+        out = np.concatenate(parts, axis=2)
 
     rng = np.random.default_rng(seed)
     q, k, v = (oracle.round_to(dtype, rng.standard_normal((1, H, T, 64), np.float32)) for _ in range(3))
