@@ -105,15 +105,40 @@ hs_status attention_impl(hs_ctx* ctx, const void* q, const void* k, const void* 
   const uint64_t n = static_cast<uint64_t>(S) * H * T * D;
   if (n == 0) return HS_OK;
   if (!q || !k || !v || !out) return fail(HS_ERR_INVALID, std::string(name) + ": null tensor pointer");
-  if (D != 64)
+  if (D != 64 && D != 128)
     return fail(HS_ERR_UNSUPPORTED,
-                std::string(name) + ": head_dim " + std::to_string(D) + " unsupported (this build implements 64)");
+                std::string(name) + ": head_dim " + std::to_string(D) + " unsupported (this build implements 64, 128)");
   if (static_cast<uint64_t>(S) * H > 65535u)
     return fail(HS_ERR_INVALID, std::string(name) + ": S*H > 65535 (attention grid y overflow)");
   if (T > (1u << 30)) return fail(HS_ERR_INVALID, std::string(name) + ": T too large");
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
     return fail(HS_ERR_INVALID, std::string(name) + ": tensor pointers must be 16-byte aligned");
   if (!(scale > 0.f) || !isfinite(scale)) scale = 1.0f / sqrtf(static_cast<float>(D));
+  if (D == 128) {
+    // The camera head's variant (ops.rs:236): no QK-norm or RoPE in its blocks.
+    if (qp.ln || qp.rope || kp.ln || kp.rope)
+      return fail(HS_ERR_UNSUPPORTED, std::string(name) + ": QK-norm/RoPE prologue needs head_dim 64");
+    DeviceGuard guard(ctx->device);
+    cudaStream_t st = ctx_stream(ctx);
+    const RowLayout l128 = merged ? RowLayout{static_cast<uint64_t>(H) * 128, 128, static_cast<uint64_t>(T) * H * 128}
+                                  : RowLayout{128, static_cast<uint64_t>(T) * 128, static_cast<uint64_t>(H) * T * 128};
+    AttnIO io;
+    io.q = q;
+    io.lq = l128;
+    io.k = k;
+    io.lk = l128;
+    io.v = v;
+    io.lv = l128;
+    io.out = out;
+    io.lo = l128;
+    io.out_code = static_cast<int>(dtype);
+    cudaError_t e;
+    {
+      ProfScope prof(ctx, st, "attention_d128");
+      e = launch_attention_d128(st, static_cast<int>(dtype), io, S, H, T, scale);
+    }
+    return e == cudaSuccess ? HS_OK : cuda_fail(e, name);
+  }
 
   DeviceGuard guard(ctx->device);
   cudaStream_t st = ctx_stream(ctx);

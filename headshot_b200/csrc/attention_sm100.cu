@@ -84,7 +84,7 @@ __host__ __device__ constexpr uint32_t col_s(int wg, int buf) { return static_ca
 __host__ __device__ constexpr uint32_t col_o(int wg) { return static_cast<uint32_t>(4 * kBN + 64 * wg); }
 static_assert(4 * kBN + 2 * 64 <= 512, "TMEM budget");
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: p <= 2^8 between rescales
-constexpr int kEmuPer8 = 1;                // of every 8 exponential pairs, this many run on the FMA pipe
+constexpr int kEmuPer8 = 2;                // of every 8 exponential pairs, this many run on the FMA pipe
 
 // Site codes written to the status word when a bounded wait gives up.
 enum : int {

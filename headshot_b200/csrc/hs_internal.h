@@ -84,6 +84,11 @@ struct AttnIO {
 // kernel unless `norm2_shared`: then the caller guarantees they bound every
 // launch that carries the same state `st` (all ring steps) and resets them.
 // S sequences of H heads; the state arrays are indexed head-major.
+// head_dim 128 (the camera head's attention), f32 arithmetic on the CUDA
+// cores; q/k/v/out of storage type `code` (kF32/kF16/kBF16) at the strides of
+// their RowLayouts (rows of 128 elements).
+cudaError_t launch_attention_d128(cudaStream_t stream, int code, const AttnIO& io, uint32_t S, uint32_t H, uint32_t T,
+                                  float scale);
 cudaError_t launch_attention_sm100(cudaStream_t stream, int elem, const AttnIO& io, uint32_t S, uint32_t H,
                                    uint32_t t_q, uint32_t t_kv, float scale, const AttnState& st, uint32_t max_ctas,
                                    int* status, uint32_t* sched, unsigned int* qk_norm2, bool norm2_shared,

@@ -123,6 +123,21 @@ def test_attention_matches_naive_softmax(t):
     assert np.abs(got - want).max() < 1e-4
 
 
+@pytest.mark.parametrize("t", [17, 150])
+def test_attention_d128_matches_naive_softmax(t):
+    """The camera head's head_dim-128 variant (attention.wesl with DV = 32) on the
+    kernels.rs inputs, against a float64 softmax(q k^T / sqrt(128)) v."""
+    s, h, d = 1, 2, 128
+    vals = oracle.rng_uniform(5 + t, 3 * s * h * t * d)
+    n = s * h * t * d
+    q, k, v = (vals[i * n:(i + 1) * n].reshape(s, h, t, d) for i in range(3))
+    got = oracle.attention(q, k, v)
+    sc = np.einsum("shtd,shud->shtu", q.astype(np.float64), k.astype(np.float64)) / np.sqrt(128.0)
+    p = np.exp(sc - sc.max(-1, keepdims=True))
+    want = np.einsum("shtu,shud->shtd", p / p.sum(-1, keepdims=True), v.astype(np.float64))
+    assert np.abs(got - want).max() < 1e-4
+
+
 def test_attention_rows_equal_full():
     rng = np.random.default_rng(0)
     q, k, v = (rng.standard_normal((2, 3, 130, 64), np.float32) for _ in range(3))
