@@ -106,10 +106,13 @@ HS_API hs_status hs_sync(hs_ctx* ctx);
 /* -------------------------------------------------------------- ops ---- */
 
 /* Replaces GpuContext::attention (src/engine/ops.rs:228-253).
- * q, k, v, out: (S, H, T, D) of `dtype`; D must be 64; S*H <= 65535.
+ * q, k, v, out: (S, H, T, D) of `dtype`; D is 64 or 128; S*H <= 65535.
  * scale <= 0 selects 1/sqrt(D) as the reference does (ops.rs:244).
- * f16/bf16 inputs compute on tcgen05 in that type with f32 softmax;
- * f32 inputs are rounded to bf16 for the tensor core, out stays f32. */
+ * D = 64: f16/bf16 inputs compute on tcgen05 in that type with f32
+ * softmax; f32 inputs are rounded to bf16 for the tensor core, out stays
+ * f32.  D = 128 (the camera head's "attention_d128", ops.rs:236): f32
+ * arithmetic for every storage type; the fused entry points take it only
+ * without a QK-norm/RoPE prologue (the camera head has none). */
 HS_API hs_status hs_attention(hs_ctx* ctx, const void* q, const void* k, const void* v, void* out, uint32_t S, uint32_t H,
                        uint32_t T, uint32_t D, hs_dtype dtype, float scale);
 
