@@ -69,7 +69,7 @@ WORKLOADS = {
 
 
 # DRAM bytes (read + write) per attention launch, one-pass ncu captures.
-MEASURED_TRAFFIC = {"global": 12.26e9 + 574.90e6, "global43k": 271.62e6 + 74.69e6}
+MEASURED_TRAFFIC = {"global": 12.26e9 + 574.90e6, "global43k": 270.41e6 + 75.09e6}
 
 
 def log(*a):
