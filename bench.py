@@ -61,6 +61,12 @@ WORKLOADS = {
     "aggregator": dict(kind="aggregator", frames=100, size=518, dtype="bf16", seed=4,
                        name="VGGT-1B aggregator forward, 100 frames 518x518 (patch 14, 37x37, 5 prefix tokens), "
                             "bf16, random-init N(0,0.02), LayerScale 1e-5"),
+    # BASELINE config 1's shape: one frame block + one global block over 4 frames x 1374 tokens,
+    # dim 1024, random weights N(0,0.02), LayerScale 1e-5, QK-LN eps 1e-6, seed 0 (the reference
+    # runs it f32 on lavapipe; here bf16 storage, the tensor-core path).
+    "block_pair": dict(kind="block_pair", frames=4, t=1374, dtype="bf16", seed=0,
+                       name="VGGT block pair (frame block + global block), 4 frames x 1374 tokens, dim 1024, "
+                            "16 heads x 64, MLP 4096, bf16, random-init N(0,0.02), LayerScale 1e-5"),
     "frame_block": dict(S=200, H=16, frames=1, T_f=1374, dtype="f16", seed=2, prefix=5, grid=(37, 37), eps=1e-6,
                         layout="block",
                         name="batched frame attention on the projection layout (S*T, H*D) in and merged out, "
@@ -735,15 +741,28 @@ def run_aggregator(args, wl: dict, rank: int, world: int, local: int) -> dict | 
     all_ms, all_n = ctx.prof_read("*")
     value = n_total / (ms / 1e3)
 
-    # end to end: the rank's images up from pinned host memory, its four caches down
+    # end to end: the rank's images up from pinned host memory, its four caches down; each
+    # cache's download starts on a copy stream as soon as the cache is built, overlapping the
+    # layers after it
     ih = images.cpu().pin_memory()
     ch = [torch.empty(c.shape, dtype=c.dtype).pin_memory() for c in caches]
+    copy_stream = torch.cuda.Stream(dev)
 
     def e2e_step():
         ctx.upload(images, ih)
-        out = step()
-        for hbuf, c in zip(ch, out):
-            ctx.download(hbuf, c)
+        built = []
+
+        def tap(name, t):
+            if name.startswith("cache."):
+                ev = torch.cuda.Event()
+                ev.record(stream)
+                with torch.cuda.stream(copy_stream):
+                    copy_stream.wait_event(ev)
+                    ctx.download(ch[len(built)], t)
+                built.append(t)
+
+        out = agg.forward(ctx, images, tap=tap, ring=ring, n_total=n_total, frame0=f0)
+        stream.wait_stream(copy_stream)
         return out
 
     del caches
@@ -801,6 +820,182 @@ def run_aggregator(args, wl: dict, rank: int, world: int, local: int) -> dict | 
         }
     ctx.close()
     return result
+
+
+def _block_pair_setup(wl: dict, dev, tdt):
+    import torch
+
+    from headshot_b200 import rope as rope_mod
+    from headshot_b200.aggregator import AggregatorConfig, Block, BlockWeights
+    from headshot_b200.engine import Rope
+
+    cfg = AggregatorConfig()
+    g = torch.Generator(device=dev).manual_seed(wl["seed"])
+    frame_blk = Block(BlockWeights.random(cfg, True, tdt, g, dev), cfg.heads, cfg.norm_eps)
+    global_blk = Block(BlockWeights.random(cfg, True, tdt, g, dev), cfg.heads, cfg.norm_eps)
+    n, t = wl["frames"], wl["t"]
+    x = torch.randn((n * t, cfg.dim), generator=g, device=dev).to(tdt)
+    sin, cos = rope_mod.tables(None, 37, 37)
+    rope = Rope(torch.from_numpy(sin).to(dev), torch.from_numpy(cos).to(dev), t - 37 * 37, t)
+    return cfg, frame_blk, global_blk, x, rope
+
+
+def _block_pair_flops(cfg, n: int, t: int) -> float:
+    d, hid = cfg.dim, cfg.mlp_hidden
+    gemm = 2.0 * n * t * (4 * d * d + 2 * d * hid)
+    return 2 * gemm + 4.0 * n * cfg.heads * t * t * 64 + 4.0 * cfg.heads * (n * t) ** 2 * 64
+
+
+def run_block_pair(args, wl: dict, rank: int, world: int, local: int) -> dict | None:
+    """Config 1's block pair through Block.forward (hs_layernorm, hs_linear, hs_attention_block_fused);
+    too small to shard, so at N > 1 every rank runs a replica (weak scaling)."""
+    import torch
+
+    from headshot_b200.engine import GpuContext
+
+    tdt = {"bf16": torch.bfloat16, "f16": torch.float16}[wl["dtype"]]
+    ctx = GpuContext(local)
+    dev = torch.device("cuda", local)
+    cfg, fb, gb, x, rope = _block_pair_setup(wl, dev, tdt)
+    n, t = wl["frames"], wl["t"]
+
+    def step(xx=x):
+        return gb.forward(ctx, fb.forward(ctx, xx, n, t, rope), 1, n * t)
+
+    fl = _block_pair_flops(cfg, n, t)
+    stream = torch.cuda.current_stream(dev)
+    # 5.6k tokens of activations fit in L2: a 256 MB write between steps evicts them
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for _ in range(args.warmup):
+        step()
+    ctx.sync()
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(gpu_id_for_smi(local))
+    sampler.start()
+    time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    for i in range(args.steps):
+        flush.fill_(i & 0xFF)
+        starts[i].record(stream)
+        step()
+        ends[i].record(stream)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    clocks = sampler.stop()
+    ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in zip(starts, ends)), world) / args.steps
+    value = fl * world / (ms / 1e3) / 1e12
+
+    xh = x.cpu().pin_memory()
+    out = step()
+    oh = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+
+    def e2e_step():
+        ctx.upload(x, xh)
+        o = step()
+        ctx.download(oh, o)
+
+    for i in range(args.steps):
+        flush.fill_(i & 0xFF)
+        starts[i].record(stream)
+        e2e_step()
+        ends[i].record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in zip(starts, ends)), world) / args.steps
+    peaks = measured_peaks()
+    result = None
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            fl_s, dt = cpu_block_pair_sample(wl, fb, gb, x, args.cpu_threads or _threads())
+            cpu = {"value": round(fl_s / dt / 1e12, 6), "unit": "TFLOP/s", "cores": args.cpu_threads or _threads(),
+                   "kind": "port", "sample": f"one frame of the frame block and the global block's rows of that frame "
+                                             f"(all 5496 keys), f32 oracle, {dt:.1f} s"}
+        result = {
+            "metric": "block pair TFLOP/s (BASELINE config 1 shape: frame block + global block, 4 frames)",
+            "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": wl["dtype"], "data": f"synthetic x N(0,1), random-init weights N(0,0.02), seed {wl['seed']}",
+            "config": {"workload": wl["name"], "tokens": n * t, "tokens_per_s": round(n * t * world / (ms / 1e3)),
+                       "flops_per_step": fl, "parallelism": f"replicas x{world}",
+                       "l2": "256 MB buffer written between timed steps (activations fit in L2)"},
+            "roofline": {"bound": "tensor", "achieved": round(fl / (ms / 1e3) / 1e12, 1), "peak": peaks["bf16"],
+                         "unit": "TFLOP/s", "frac": round(fl / (ms / 1e3) / 1e12 / peaks["bf16"], 4),
+                         "traffic": None, "peak_source": f"{peaks['source']} bf16 burst (MEASURED_PEAKS.json)",
+                         "kernel": "whole step (14 launches: attention, linears, LayerNorms, QK prep)"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(fl * world / (e2e_ms / 1e3) / 1e12, 2), "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": x.numel() * x.element_size() * world,
+                    "d2h_bytes_per_step": out.numel() * out.element_size() * world, "ms_per_step": round(e2e_ms, 4)},
+            "gpu_launches": 14 * args.steps * world,
+            "clocks": clocks,
+        }
+    ctx.close()
+    return result
+
+
+def _np_block(b) -> dict:
+    a = lambda t: t.float().cpu().numpy()  # noqa: E731
+    w = b.w
+    qn = None if w.qk_norm is None else (a(w.qk_norm.q_w), a(w.qk_norm.q_b), a(w.qk_norm.k_w), a(w.qk_norm.k_b),
+                                         w.qk_norm.eps)
+    return {"norm1_w": a(w.norm1_w), "norm1_b": a(w.norm1_b), "qkv_w": [a(y) for y in w.qkv_w],
+            "qkv_b": [a(y) for y in w.qkv_b], "proj_w": a(w.proj_w), "proj_b": a(w.proj_b), "ls1": a(w.ls1),
+            "norm2_w": a(w.norm2_w), "norm2_b": a(w.norm2_b), "fc1_w": a(w.fc1_w), "fc1_b": a(w.fc1_b),
+            "fc2_w": a(w.fc2_w), "fc2_b": a(w.fc2_b), "ls2": a(w.ls2), "qk_norm": qn}
+
+
+def cpu_block_pair_sample(wl: dict, fb, gb, x, threads: int, np_blocks: tuple | None = None) -> tuple[float, float]:
+    """The reference path (oracle restatements, f32, reference op order) on a bounded,
+    exactly counted quarter of config 1: frame 0 through the frame block, then the global
+    block for frame 0's rows (LayerNorm, q/proj/MLP linears on those rows; k/v linears on
+    all 5496 rows; attention of those rows over every key).  Returns (FLOPs, seconds)."""
+    import numpy as np
+
+    import oracle
+    from oracle import model as om
+
+    n, t = wl["frames"], wl["t"]
+    d, heads = 1024, 16
+    fbn, gbn = np_blocks or (_np_block(fb), _np_block(gb))
+    xs = x.float().cpu().numpy()
+    sin, cos = oracle.rope_tables(37, 37)
+    prefix = t - 37 * 37
+
+    def r(a):
+        return oracle.round_to(wl["dtype"], a)
+
+    t0 = time.perf_counter()
+    frame0 = om.block_forward(xs[:t], fbn, 1, t, heads, 1e-5, wl["dtype"], (sin, cos, prefix))
+    # the other frames' frame-block outputs are inputs to the global block: taken as the
+    # (untimed) rounded input rows, the sample's cost is frame 0's
+    xg = np.concatenate([frame0, r(xs[t:])])
+    normed = r(oracle.layernorm(xg, gbn["norm1_w"], gbn["norm1_b"], 1e-5))
+    q = r(oracle.linear(normed[:t], gbn["qkv_w"][0], gbn["qkv_b"][0], nthreads=threads))
+    k = r(oracle.linear(normed, gbn["qkv_w"][1], gbn["qkv_b"][1], nthreads=threads))
+    v = r(oracle.linear(normed, gbn["qkv_w"][2], gbn["qkv_b"][2], nthreads=threads))
+    qw, qb, kw, kb, eps = gbn["qk_norm"]
+    qh = r(oracle.layernorm(oracle.split_heads(q, 1, t, heads, 64), qw, qb, eps))
+    kh = r(oracle.layernorm(oracle.split_heads(k, 1, n * t, heads, 64), kw, kb, eps))
+    vh = oracle.split_heads(v, 1, n * t, heads, 64)
+    # rows of frame 0 (head-major, per head over every key)
+    qpad = np.zeros((1, heads, n * t, 64), np.float32)
+    qpad[:, :, :t] = qh
+    rows = np.concatenate([np.arange(t) + h * n * t for h in range(heads)])
+    att = oracle.attention_rows(qpad, kh, vh, rows, nthreads=threads).reshape(heads, t, 64)
+    merged = r(oracle.attn_merge(att[None]))
+    x1 = r(oracle.residual_ls(xg[:t], r(oracle.linear(merged, gbn["proj_w"], gbn["proj_b"], nthreads=threads)),
+                              gbn["ls1"]))
+    h2 = r(oracle.layernorm(x1, gbn["norm2_w"], gbn["norm2_b"], 1e-5))
+    hid = r(oracle.gelu(r(oracle.linear(h2, gbn["fc1_w"], gbn["fc1_b"], nthreads=threads))))
+    oracle.residual_ls(x1, r(oracle.linear(hid, gbn["fc2_w"], gbn["fc2_b"], nthreads=threads)), gbn["ls2"])
+    dt = time.perf_counter() - t0
+    gemm_rows = 2.0 * t * (4 * d * d + 2 * d * 4096)  # frame block on frame 0
+    gemm_glob = 2.0 * t * d * d * 2 + 2.0 * n * t * d * d * 2 + 2.0 * t * 2 * d * 4096  # q, proj; k, v; fc1, fc2
+    flops = gemm_rows + 4.0 * heads * t * t * 64 + gemm_glob + 4.0 * heads * t * n * t * 64
+    return flops, dt
 
 
 def cpu_aggregator_estimate(cfg, frames: int, size: int, threads: int, dtype: str, seconds: float = 12.0) -> dict:
@@ -992,6 +1187,39 @@ def run_reference_aggregator(args, wl: dict) -> dict:
             "e2e": {"value": round(value, 8), "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+def run_reference_block_pair(args, wl: dict) -> dict:
+    """Config 1 on the CPU: the oracle composition of Block::forward on the bounded quarter
+    sample of cpu_block_pair_sample, each step one sample."""
+    import torch
+
+    from headshot_b200.aggregator import AggregatorConfig, Block, BlockWeights
+
+    threads = args.cpu_threads or _threads()
+    cfg = AggregatorConfig()
+    tdt = {"bf16": torch.bfloat16, "f16": torch.float16}[wl["dtype"]]
+    g = torch.Generator().manual_seed(wl["seed"])  # CPU generator: the same shapes and distribution
+    fb = Block(BlockWeights.random(cfg, True, tdt, g, torch.device("cpu")), cfg.heads, cfg.norm_eps)
+    gb = Block(BlockWeights.random(cfg, True, tdt, g, torch.device("cpu")), cfg.heads, cfg.norm_eps)
+    x = torch.randn((wl["frames"] * wl["t"], cfg.dim), generator=g).to(tdt)
+    blocks = (_np_block(fb), _np_block(gb))
+    for _ in range(min(args.warmup, 1)):
+        cpu_block_pair_sample(wl, fb, gb, x, threads, blocks)
+    fl = dt = 0.0
+    for _ in range(args.steps):
+        f, d = cpu_block_pair_sample(wl, fb, gb, x, threads, blocks)
+        fl += f
+        dt += d
+    value = fl / dt / 1e12
+    return {"impl": "reference", "metric": "block pair TFLOP/s (BASELINE config 1 shape: frame block + global "
+            "block, 4 frames)", "value": round(value, 6), "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 1), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": f"synthetic, rounded to {wl['dtype']}",
+            "config": {"workload": wl["name"]},
+            "cpu_baseline": {"value": round(value, 6), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                             "sample": "per step one quarter of the block pair (frame 0's rows; every key)"},
+            "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
 def run_reference_glue(args, wl: dict) -> dict:
     """The trunk glue on the CPU (the oracle's numpy restatement of copy_rows,
     concat_channels and cast_to_f32) over a bounded sample of frames."""
@@ -1066,6 +1294,8 @@ def main():
             ref = run_reference_glue(args, wl)
         elif wl.get("kind") == "aggregator":
             ref = run_reference_aggregator(args, wl)
+        elif wl.get("kind") == "block_pair":
+            ref = run_reference_block_pair(args, wl)
         else:
             ref = run_reference_mlp(args, wl) if wl.get("kind") == "mlp" else run_reference(args, wl)
         print(json.dumps(ref), file=out, flush=True)
@@ -1076,7 +1306,8 @@ def main():
         log(f"note: --gpus {args.gpus} but WORLD_SIZE {world}; using {world}")
     try:
         kind = wl.get("kind")
-        runner = {"mlp": run_mlp, "glue": run_glue, "aggregator": run_aggregator}.get(kind, run_ours)
+        runner = {"mlp": run_mlp, "glue": run_glue, "aggregator": run_aggregator,
+                  "block_pair": run_block_pair}.get(kind, run_ours)
         res = runner(args, wl, rank, world, local)
     finally:
         if world > 1:
