@@ -470,8 +470,24 @@ hs_status hs_linear(hs_ctx* ctx, const void* x, const void* w, const float* bias
   if (!ctx) return fail(HS_ERR_INVALID, std::string(name) + ": null context");
   if (!valid_dtype(dtype)) return fail(HS_ERR_INVALID, std::string(name) + ": unknown dtype");
   if (M == 0 || N == 0) return HS_OK;
-  if (dtype == HS_F32)
-    return fail(HS_ERR_UNSUPPORTED, std::string(name) + ": f32 storage is not implemented (f16/bf16 only)");
+  if (dtype == HS_F32) {  // the reference's f32 linear: f32 arithmetic, any shape
+    if (K == 0) return fail(HS_ERR_INVALID, std::string(name) + ": K must be non-zero");
+    if (epilogue < HS_LINEAR_PLAIN || epilogue > HS_LINEAR_RESIDUAL_LS)
+      return fail(HS_ERR_INVALID, std::string(name) + ": unknown epilogue");
+    if (!x || !w || !out) return fail(HS_ERR_INVALID, std::string(name) + ": null tensor pointer");
+    if (epilogue == HS_LINEAR_RESIDUAL_LS && (!residual || !gamma))
+      return fail(HS_ERR_INVALID, std::string(name) + ": the residual epilogue needs residual and gamma");
+    if ((M + 127) / 128 > 65535u) return fail(HS_ERR_INVALID, std::string(name) + ": M > 65535 * 128 for f32");
+    DeviceGuard guard(ctx->device);
+    cudaStream_t st = ctx_stream(ctx);
+    cudaError_t e;
+    {
+      ProfScope prof(ctx, st, "linear");
+      e = launch_linear_f32(st, static_cast<const float*>(x), static_cast<const float*>(w), bias,
+                            static_cast<float*>(out), M, K, N, epilogue, static_cast<const float*>(residual), gamma);
+    }
+    return e == cudaSuccess ? HS_OK : cuda_fail(e, name);
+  }
   if (K == 0 || K % 8 || N % 8)
     return fail(HS_ERR_UNSUPPORTED, std::string(name) + ": K and N must be non-zero multiples of 8 (16-byte rows)");
   if (epilogue < HS_LINEAR_PLAIN || epilogue > HS_LINEAR_RESIDUAL_LS)

@@ -117,6 +117,11 @@ cudaError_t launch_linear_sm100(cudaStream_t stream, int elem, const void* x, co
                                 void* out, uint64_t m, uint32_t k, uint32_t n, int epi, const void* res,
                                 const float* gamma, int* status, uint64_t timeout_ns, std::string* err);
 
+// The same op for f32 storage, f32 arithmetic on the CUDA cores (gemm_f32.cu):
+// any m, k, n; m <= 65535 * 128.
+cudaError_t launch_linear_f32(cudaStream_t stream, const float* x, const float* w, const float* bias, float* out,
+                              uint64_t m, uint32_t k, uint32_t n, int epi, const float* res, const float* gamma);
+
 // One tensor of a qk_prep launch: x (S, H, T, 64) in layout `lx` in, head-
 // major rows out, with its own prologue.
 struct PrepJob {

@@ -181,7 +181,9 @@ HS_API hs_status hs_attention_fused_noalloc(void* stream, int* status, const voi
  *                         shaders/residual_ls.wesl); residual (M, N), gamma (N, f32).
  * f16/bf16 storage on tcgen05 with f32 accumulation (the fused epilogue
  * works on the f32 sum; the reference rounds the linear's output first).
- * K and N must be multiples of 8; f32 storage returns HS_ERR_UNSUPPORTED.
+ * K and N must be multiples of 8 for 16-bit storage.  f32 storage (the
+ * reference's DINO and camera head) computes in f32 on the CUDA cores, any
+ * K and N, M <= 65535 * 128.
  * All pointers 16-byte aligned; bias may be NULL.  out may alias residual. */
 #define HS_LINEAR_PLAIN 0
 #define HS_LINEAR_GELU 1

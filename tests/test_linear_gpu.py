@@ -1,4 +1,5 @@
-"""The block's linears on tcgen05 (hs_linear) against the CPU oracle.
+"""The block's linears (hs_linear: tcgen05 for f16/bf16, f32 on the CUDA cores)
+against the CPU oracle.
 
 Restated cases from the reference's own tests (tests/kernels.rs:313-374,
 linear_f16_and_wmma_match_cpu: f16-rounded inputs, f64 sums, f16 output,
@@ -101,11 +102,47 @@ def test_linear_residual_ls_epilogue(gpu_ctx, dtype, inplace):
     close(out.float().cpu().numpy(), ref, _tol(dtype))
 
 
+def test_linear_reference_f32_case(gpu_ctx):
+    """kernels.rs:63-100 (linear_matches_cpu): Rng(2), (m, k, n) = (37, 53, 29), f32, against
+    f64 sums with and without bias, tolerance 1e-4 (abs + rel, kernels.rs:35-43)."""
+    m, k, n = 37, 53, 29
+    vals = oracle.rng_uniform(2, m * k + n * k + n)
+    x = vals[:m * k].reshape(m, k)
+    w = vals[m * k:m * k + n * k].reshape(n, k)
+    b = vals[m * k + n * k:]
+    exp = (x.astype(np.float64) @ w.astype(np.float64).T).astype(np.float32) + b
+    xd, wd = torch.from_numpy(x).cuda(), torch.from_numpy(w).cuda()
+    out = gpu_ctx.linear(xd, wd, torch.from_numpy(b).cuda())
+    out_nb = gpu_ctx.linear(xd, wd)
+    gpu_ctx.sync()
+    close(out.cpu().numpy(), exp, 1e-4)
+    close(out_nb.cpu().numpy(), exp - b, 1e-4)
+
+
+@pytest.mark.parametrize("epilogue", ["none", "gelu", "residual_ls"])
+@pytest.mark.parametrize("m,k,n", [(300, 1024, 1024), (129, 768, 4096), (1, 1, 1), (257, 130, 67)])
+def test_linear_f32(gpu_ctx, epilogue, m, k, n):
+    rng = np.random.default_rng(m + k + n)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    w = (rng.standard_normal((n, k)) / np.sqrt(k)).astype(np.float32)
+    b = (0.1 * rng.standard_normal(n)).astype(np.float32)
+    ref = oracle.linear(x, w, b)
+    kw = {}
+    if epilogue == "gelu":
+        ref = oracle.gelu(ref)
+    elif epilogue == "residual_ls":
+        res = rng.standard_normal((m, n)).astype(np.float32)
+        gamma = (0.5 * rng.standard_normal(n)).astype(np.float32)
+        ref = oracle.residual_ls(res, ref, gamma)
+        kw = {"residual": torch.from_numpy(res).cuda(), "gamma": torch.from_numpy(gamma).cuda()}
+    out = gpu_ctx.linear(torch.from_numpy(x).cuda(), torch.from_numpy(w).cuda(), torch.from_numpy(b).cuda(),
+                         epilogue=epilogue, **kw)
+    gpu_ctx.sync()
+    close(out.cpu().numpy(), ref, 1e-5)
+
+
 def test_linear_rejects_unsupported(gpu_ctx):
     x = torch.zeros((4, 12), device="cuda", dtype=torch.float16)  # K = 12: not a multiple of 8
     w = torch.zeros((16, 12), device="cuda", dtype=torch.float16)
     with pytest.raises(_lib.HsError):
         gpu_ctx.linear(x, w)
-    xf = torch.zeros((4, 16), device="cuda", dtype=torch.float32)
-    with pytest.raises(_lib.HsError):
-        gpu_ctx.linear(xf, torch.zeros((16, 16), device="cuda", dtype=torch.float32))
