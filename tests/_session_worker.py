@@ -9,6 +9,9 @@ the oracle's attention for this rank's query rows.
 
 mode "preflight": rank 1 leaves right after joining; rank 0's
 session.preflight() must raise instead of waiting forever.
+
+mode "drop": the ring's block exchange with one message dropped (the last
+rank leaves instead of sending); the other ranks' exchanges must fail.
 """
 from __future__ import annotations
 
@@ -101,19 +104,50 @@ def preflight(rank: int, world: int) -> int:
     return 1
 
 
+def drop(rank: int, world: int) -> int:
+    """The last rank drops the [K|V] block it owes its successor after step 0
+    and leaves; every other rank must see its next exchange fail (an
+    exception within the group timeout) instead of waiting forever."""
+    import torch
+    import torch.distributed as dist
+
+    from headshot_b200 import session
+
+    H, T, D = 2, 64, 64
+    t0, t1 = session.ring_shard(T, world, rank)
+    block = torch.full((2 * H * (t1 - t0) * D,), float(rank))
+    try:
+        for step in range(world - 1):
+            plan = session.ring_plan(rank, world, step)
+            if rank == world - 1 and step == 0:
+                os._exit(0)  # the message to send_to is dropped; this rank is gone
+            n0, n1 = session.ring_shard(T, world, (plan["src"] - 1) % world)
+            recv = torch.empty(2 * H * (n1 - n0) * D)
+            ops = [dist.P2POp(dist.isend, block, plan["send_to"]), dist.P2POp(dist.irecv, recv, plan["recv_from"])]
+            for w in dist.batch_isend_irecv(ops):
+                w.wait()
+            block = recv
+    except Exception as e:  # noqa: BLE001
+        print(f"rank {rank}: exchange failed with {type(e).__name__}", flush=True)
+        return 0
+    print(f"rank {rank}: every exchange completed although a rank dropped its block", flush=True)
+    return 1
+
+
 def main() -> int:
     mode, rank, world, port = sys.argv[1], int(sys.argv[2]), int(sys.argv[3]), int(sys.argv[4])
     import torch.distributed as dist
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=20))
-    rc = ring(rank, world) if mode == "ring" else preflight(rank, world)
+    timeout = timedelta(seconds=10 if mode == "drop" else 20)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timeout)
     if mode == "ring":
+        rc = ring(rank, world)
         dist.destroy_process_group()
-    else:
-        os._exit(rc)
-    return rc
+        return rc
+    rc = preflight(rank, world) if mode == "preflight" else drop(rank, world)
+    os._exit(rc)
 
 
 if __name__ == "__main__":

@@ -39,3 +39,11 @@ def test_preflight_detects_a_departed_rank():
     """A rank that leaves between steps is noticed on the host before ring traffic."""
     rcs = _run("preflight", 2, timeout=120)
     assert rcs[0] == 0
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_dropped_ring_block_fails_every_waiting_rank(world):
+    """A ring block that is never sent (its owner leaves) ends the other ranks'
+    exchanges with an error within the group timeout; none waits forever."""
+    rcs = _run("drop", world, timeout=120)
+    assert rcs == [0] * world
