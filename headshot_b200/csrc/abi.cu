@@ -185,7 +185,7 @@ hs_status attention_impl(hs_ctx* ctx, const void* q, const void* k, const void* 
   if (n_jobs) {
     {
       ProfScope prof(ctx, st, "qk_prep");
-      e = launch_qk_prep(st, code, elem, S, H, T, jobs, n_jobs);
+      e = launch_qk_prep(st, code, elem, S, H, T, jobs, n_jobs, ctx->d_status, ctx_timeout_ns(ctx));
     }
     if (e != cudaSuccess) return cuda_fail(e, "qk_prep");
   }

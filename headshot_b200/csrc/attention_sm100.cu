@@ -207,24 +207,7 @@ __device__ __forceinline__ void mbar_arrive_elect(uint64_t* bar) {
       : "memory");
 }
 
-// ---- packed f32x2 arithmetic (sm_100) and the FMA-pipe exp2 -------------
-
-__device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0,
-                                     float c1) {
-  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
-      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d0), "=f"(d1)
-      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
-}
-
-__device__ __forceinline__ void add2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
-  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d0), "=f"(d1)
-      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
-}
+// ---- the FMA-pipe exp2 (packed f32x2 helpers: hs_ptx.cuh) ----------------
 
 __device__ __forceinline__ float max3(float a, float b, float c) {
   float d;
@@ -747,72 +730,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  if (!fn) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  }
-  return fn;
-}
-
 // (S, H, T, 64) 16-bit tensor in row layout `l` as a 4-D map (64, T, H, S)
-// with box_rows x 64 boxes, 128B swizzle.  Rows past T inside a sequence read
-// as zeros (out-of-bounds fill).
+// with box_rows x 64 boxes, 128B swizzle (launch_util.cu).  Rows past T
+// inside a sequence read as zeros (out-of-bounds fill).
 bool make_map(CUtensorMap* map, const void* base, const RowLayout& l, bool bf16, uint32_t t, uint32_t heads,
               uint32_t seqs, uint32_t box_rows, std::string* err) {
-  EncodeTiledFn fn = encode_fn();
-  if (!fn) {
-    if (err) *err = "cuTensorMapEncodeTiled unavailable";
-    return false;
-  }
-  cuuint64_t dims[4] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(t), static_cast<cuuint64_t>(heads),
-                        static_cast<cuuint64_t>(seqs)};
-  cuuint64_t strides[3] = {static_cast<cuuint64_t>(l.t) * 2, static_cast<cuuint64_t>(l.h) * 2,
-                           static_cast<cuuint64_t>(l.s) * 2};
-  cuuint32_t box[4] = {static_cast<cuuint32_t>(kD), box_rows, 1, 1};
-  cuuint32_t estr[4] = {1, 1, 1, 1};
-  CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
-                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) {
-    if (err) *err = "cuTensorMapEncodeTiled failed with code " + std::to_string(static_cast<int>(r));
-    return false;
-  }
-  return true;
+  return make_row_map(map, base, l, bf16, t, heads, seqs, box_rows, err);
 }
 
-int sm_count_of_current_device() {
-  static std::mutex mu;
-  static int cache[64] = {0};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  std::lock_guard<std::mutex> lock(mu);
-  if (!cache[dev]) {
-    int n = 0;
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-    cache[dev] = n;
-  }
-  return cache[dev];
-}
+int sm_count_of_current_device() { return current_sm_count(); }
 
 template <typename E>
 cudaError_t launch_typed(cudaStream_t stream, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                          const Args& a, uint32_t ctas) {
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e =
-        cudaFuncSetAttribute(attn_fwd_sm100<E>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  const cudaError_t e =
+      ensure_dynamic_smem(reinterpret_cast<const void*>(attn_fwd_sm100<E>), static_cast<int>(kSmemBytes));
+  if (e != cudaSuccess) return e;
   attn_fwd_sm100<E><<<ctas, kThreads, kSmemBytes, stream>>>(mq, mk, mv, a);
   return cudaGetLastError();
 }

@@ -355,22 +355,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  });
-  return fn;
-}
+EncodeTiledFn encode_fn() { return encode_tiled_fn(); }
 
 // Row-major (rows, cols) 16-bit output as a 2-D map with 32x32 boxes, no
 // swizzle (the epilogue's staging layout).
@@ -434,13 +419,9 @@ int sm_count() {
 template <typename E>
 cudaError_t launch_typed(cudaStream_t stream, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo,
                          const Args& a, uint32_t ctas) {
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e =
-        cudaFuncSetAttribute(gemm_sm100<E>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  const cudaError_t e =
+      ensure_dynamic_smem(reinterpret_cast<const void*>(gemm_sm100<E>), static_cast<int>(kSmemBytes));
+  if (e != cudaSuccess) return e;
   gemm_sm100<E><<<ctas, kThreads, kSmemBytes, stream>>>(ma, mb, mo, a);
   return cudaGetLastError();
 }

@@ -1,6 +1,7 @@
 // hs_internal.h — launchers shared between the kernel files and the C ABI.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -72,6 +73,27 @@ struct AttnIO {
   int out_code = 0;
 };
 
+// cuTensorMapEncodeTiled, looked up once through the runtime's driver entry
+// point (null if the driver does not provide it).
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_tiled_fn();
+
+// (S, H, T, 64) 16-bit rows in layout `l` as a 4-D tensor map (64, T, H, S)
+// with box_rows x 64 boxes and 128-byte swizzle; rows past T inside a
+// sequence read as zeros.  base must be 16-byte aligned and the strides of
+// `l` multiples of 8 elements.
+bool make_row_map(CUtensorMap* map, const void* base, const RowLayout& l, bool bf16, uint32_t t, uint32_t heads,
+                  uint32_t seqs, uint32_t box_rows, std::string* err);
+
+// SMs of the current device (cached per device; 148 if the query fails).
+int current_sm_count();
+
+// Raises `func`'s dynamic shared-memory limit to `bytes` on the current
+// device (once per kernel and device).
+cudaError_t ensure_dynamic_smem(const void* func, int bytes);
+
 // Flash attention on tcgen05 (D = 64), persistent: at most `max_ctas` CTAs
 // (0 = one per SM) take the (sequence, 256-row) work items from the counter
 // pair `sched` (2 x u32, zero before the launch; the kernel leaves it zero,
@@ -135,13 +157,17 @@ struct PrepJobs {
   PrepJob job[kMaxPrepJobs];
 };
 // Up to kMaxPrepJobs tensors of the same shape and types in one launch.
+// 16-bit rows in and out of the same type stream through shared memory by
+// TMA (bounded waits: on a timeout a site code goes to `status`); f32 rows
+// in or out take a register-only kernel.
 cudaError_t launch_qk_prep(cudaStream_t stream, int in_code, int out_code, uint32_t S, uint32_t H, uint32_t t,
-                           const PrepJob* jobs, int n_jobs);
+                           const PrepJob* jobs, int n_jobs, int* status, uint64_t timeout_ns);
 
 // Reads x (S, H, T, 64) in layout `lx`, writes head-major 16-bit or f32
 // rows.
 cudaError_t launch_qk_prep(cudaStream_t stream, const void* x, int in_code, const RowLayout& lx, void* out,
-                           int out_code, uint32_t S, uint32_t H, uint32_t t, const QkPrologue& p);
+                           int out_code, uint32_t S, uint32_t H, uint32_t t, const QkPrologue& p, int* status,
+                           uint64_t timeout_ns);
 
 // Companion ops of the reference engine.
 cudaError_t launch_layernorm(cudaStream_t stream, const void* x, void* out, int code, const float* w,

@@ -156,7 +156,7 @@ extern "C" hs_status hs_attention_fused_noalloc(void* stream, int* status, const
     kp.norm2_max = p.sched + 3;
     const hs::RowLayout hm = hs::RowLayout::head_major(H, T);
     const hs::PrepJob jobs[2] = {{q, hm, q_rows, qp}, {k, hm, k_rows, kp}};
-    e = hs::launch_qk_prep(st, code, code, S, H, T, jobs, 2);
+    e = hs::launch_qk_prep(st, code, code, S, H, T, jobs, 2, status_word, kNoAllocTimeoutNs);
     if (e != cudaSuccess) return hs::abi_cuda_fail(e, name);
     q_use = q_rows;
     k_use = k_rows;

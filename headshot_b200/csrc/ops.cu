@@ -275,6 +275,255 @@ __global__ void __launch_bounds__(256) qk_prep_kernel(PrepJobs jobs, uint32_t sh
   }
 }
 
+// ---- qk_prep for 16-bit rows, staged through shared memory by TMA ----------
+//
+// Work unit = 32 consecutive tokens of 8 sequences of one tensor.  A block
+// takes a contiguous range of units (sequences fastest, so a thread's folded
+// table constants, which depend on the token only, are rebuilt only when the
+// token block changes) and streams them through two shared-memory stages:
+// one thread issues the 8 TMA box loads (32 rows x 128 B each) of unit i+2
+// into the stage unit i has just released, so HBM reads stay in flight while
+// the block computes.  Thread (token, g) computes elements [4g, 4g+4) and
+// their rotate-half partners [32+4g, 36+4g) of its token's row in each
+// sequence of the unit.  LayerNorm's affine and the RoPE rotation fold into
+// three constants per output element (d = x - mean, inv = 1/sqrt(var + eps)):
+//   x'[i]    = inv * (A_lo d[i] + B_lo d[i+32]) + C_lo,   A_lo = w[i] cos[i],
+//              B_lo = -w[i+32] sin[i],  C_lo = b[i] cos[i] - b[i+32] sin[i]
+//   x'[i+32] = inv * (A_hi d[i+32] + B_hi d[i]) + C_hi,   A_hi = w[i+32] cos[i+32],
+//              B_hi = w[i] sin[i+32],   C_hi = b[i+32] cos[i+32] + b[i] sin[i+32]
+// (pass-through tokens: sin 0, cos 1; no LayerNorm: d = x, inv = 1, w = 1, b = 0).
+constexpr int kTpTokens = 32;
+constexpr int kTpSeqs = 8;
+constexpr int kTpStages = 2;
+constexpr uint32_t kTpBoxBytes = kTpTokens * 128;            // 32 rows of 64 16-bit elements
+constexpr uint32_t kTpStageBytes = kTpSeqs * kTpBoxBytes;    // 32 KiB
+constexpr int kTpThreads = kTpTokens * 8;
+constexpr int kTpBlocksPerSm = 3;
+constexpr size_t kTpSmemBytes = 1024 /*alignment slack*/ + kTpStages * kTpStageBytes + 64;
+constexpr int kSitePrepFull = 0x201;
+
+struct TmaPrepArgs {
+  PrepJobs jobs;      // x is read through the tensor maps
+  uint32_t sh;        // sequences (S * H)
+  uint32_t heads;
+  uint32_t t;
+  uint32_t n_tb;      // token blocks: ceil(t / 32)
+  uint32_t n_sc;      // sequence chunks: ceil(sh / 8)
+  uint64_t units;     // jobs * n_tb * n_sc
+  int* status;
+  uint64_t timeout_ns;
+};
+
+template <typename E>
+__global__ void __launch_bounds__(kTpThreads, kTpBlocksPerSm)
+    qk_prep_tma_kernel(const __grid_constant__ CUtensorMap tm0, const __grid_constant__ CUtensorMap tm1,
+                       const __grid_constant__ CUtensorMap tm2, const __grid_constant__ TmaPrepArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* stages = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(stages + kTpStages * kTpStageBytes);
+  int* abort_flag = reinterpret_cast<int*>(full + kTpStages);
+
+  const uint64_t u_begin = blockIdx.x * a.units / gridDim.x;
+  const uint64_t u_end = (blockIdx.x + 1ull) * a.units / gridDim.x;
+  const uint32_t per_job = a.n_tb * a.n_sc;
+
+  // Warp w, lane (j, g): token lt = (w & 3) + 4j + 16(w >> 2).  The four rows
+  // a warp reads at once are then lt, lt+4, lt+8, lt+12, whose 128-byte
+  // swizzle phases put two rows in each half of the banks (two wavefronts per
+  // 8-byte read of the warp, the minimum).
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int g = lane & 7;
+  const int lt = (warp & 3) + 4 * (lane >> 3) + 16 * (warp >> 2);
+  const uint32_t sw = static_cast<uint32_t>(lt & 7);
+  const uint32_t off_lo = static_cast<uint32_t>(lt) * 128 + ((static_cast<uint32_t>(g >> 1) ^ sw) << 4) + (g & 1) * 8;
+  const uint32_t off_hi =
+      static_cast<uint32_t>(lt) * 128 + ((static_cast<uint32_t>(4 + (g >> 1)) ^ sw) << 4) + (g & 1) * 8;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kTpStages; ++s) mbar_init(&full[s], 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  // Thread 0: the TMA loads of unit u into stage `st`.
+  auto issue = [&](uint64_t u, int st) {
+    const uint32_t job = static_cast<uint32_t>(u / per_job);
+    const uint32_t rem = static_cast<uint32_t>(u - static_cast<uint64_t>(job) * per_job);
+    const uint32_t tb = rem / a.n_sc;
+    const uint32_t q0 = (rem - tb * a.n_sc) * kTpSeqs;
+    const uint32_t nq = min(static_cast<uint32_t>(kTpSeqs), a.sh - q0);
+    const CUtensorMap* tm = job == 0 ? &tm0 : (job == 1 ? &tm1 : &tm2);
+    mbar_arrive_expect_tx(&full[st], nq * kTpBoxBytes);
+    for (uint32_t j = 0; j < nq; ++j) {
+      const uint32_t q = q0 + j;
+      tma_load_4d(tm, &full[st], stages + st * kTpStageBytes + j * kTpBoxBytes, 0,
+                  static_cast<int>(tb * kTpTokens), static_cast<int>(q % a.heads), static_cast<int>(q / a.heads));
+    }
+  };
+  uint64_t issued = u_begin;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kTpStages && issued < u_end; ++s) issue(issued++, s);
+  }
+
+  float cA[8], cB[8], cC[8];  // [0..3] lower-half outputs, [4..7] upper-half outputs
+  uint32_t cur_key = 0xffffffffu;
+  uint32_t cur_job = 0xffffffffu;
+  const PrepJob* job_p = nullptr;
+  uint32_t tok = 0;
+  bool tok_ok = false;
+  // Largest squared row norm this thread stored for the current tensor.  A
+  // block's units are tensor-major, so the tensor changes at the same unit
+  // for every thread; the block's maxima go out then (one atomic per warp,
+  // non-negative floats order like their bit patterns).
+  float n2_run = 0.f;
+  auto flush_norm = [&](uint32_t jb) {
+    unsigned int* dst = a.jobs.job[jb].p.norm2_max;
+    if (!dst) return;
+    float m = fmaxf(n2_run, __shfl_xor_sync(0xffffffffu, n2_run, 8));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
+    if (lane == 0 && m > 0.f) atomicMax(dst, __float_as_uint(m));
+  };
+
+  uint64_t i = 0;
+  for (uint64_t u = u_begin; u < u_end; ++u, ++i) {
+    const int st = static_cast<int>(i & 1);
+    const uint32_t job = static_cast<uint32_t>(u / per_job);
+    const uint32_t rem = static_cast<uint32_t>(u - static_cast<uint64_t>(job) * per_job);
+    const uint32_t tb = rem / a.n_sc;
+    const uint32_t q0 = (rem - tb * a.n_sc) * kTpSeqs;
+    const uint32_t key = job * a.n_tb + tb;
+    if (key != cur_key) {  // fold this thread's constants for (job, token)
+      cur_key = key;
+      if (job != cur_job) {
+        if (cur_job != 0xffffffffu) flush_norm(cur_job);
+        n2_run = 0.f;
+        cur_job = job;
+      }
+      job_p = &a.jobs.job[job];
+      const QkPrologue& p = job_p->p;
+      tok = tb * kTpTokens + lt;
+      tok_ok = tok < a.t;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int c = 4 * g + k;
+        float sn_lo = 0.f, sn_hi = 0.f, cs_lo = 1.f, cs_hi = 1.f;
+        if (p.rope && tok_ok) {
+          const uint32_t ft = (tok + p.pos_offset) % p.tokens_per_frame;
+          if (ft >= p.prefix) {
+            const uint64_t r = static_cast<uint64_t>(ft - p.prefix) * 64;
+            sn_lo = __ldg(p.sin_t + r + c);
+            sn_hi = __ldg(p.sin_t + r + 32 + c);
+            cs_lo = __ldg(p.cos_t + r + c);
+            cs_hi = __ldg(p.cos_t + r + 32 + c);
+          }
+        }
+        const float w_lo = p.ln ? __ldg(p.ln_w + c) : 1.f, w_hi = p.ln ? __ldg(p.ln_w + 32 + c) : 1.f;
+        const float b_lo = p.ln ? __ldg(p.ln_b + c) : 0.f, b_hi = p.ln ? __ldg(p.ln_b + 32 + c) : 0.f;
+        cA[k] = w_lo * cs_lo;
+        cB[k] = -w_hi * sn_lo;
+        cC[k] = b_lo * cs_lo - b_hi * sn_lo;
+        cA[4 + k] = w_hi * cs_hi;
+        cB[4 + k] = w_lo * sn_hi;
+        cC[4 + k] = b_hi * cs_hi + b_lo * sn_hi;
+      }
+    }
+    const QkPrologue& p = job_p->p;
+    E* __restrict__ out = static_cast<E*>(job_p->out);
+
+    const bool ok = mbar_wait(&full[st], static_cast<uint32_t>(i >> 1) & 1u, abort_flag, a.status, kSitePrepFull,
+                              a.timeout_ns);
+    if (ok) {
+      const uint8_t* box0 = stages + st * kTpStageBytes;
+      const uint32_t nq = min(static_cast<uint32_t>(kTpSeqs), a.sh - q0);
+#pragma unroll 2
+      for (uint32_t j = 0; j < nq; ++j) {
+        const uint2 rl = *reinterpret_cast<const uint2*>(box0 + j * kTpBoxBytes + off_lo);
+        const uint2 rh = *reinterpret_cast<const uint2*>(box0 + j * kTpBoxBytes + off_hi);
+        float v[8];
+        {
+          const float2 f0 = Elem<E>::unpack2(rl.x), f1 = Elem<E>::unpack2(rl.y);
+          const float2 f2 = Elem<E>::unpack2(rh.x), f3 = Elem<E>::unpack2(rh.y);
+          v[0] = f0.x; v[1] = f0.y; v[2] = f1.x; v[3] = f1.y;
+          v[4] = f2.x; v[5] = f2.y; v[6] = f3.x; v[7] = f3.y;
+        }
+        float inv = 1.f;
+        if (p.ln) {
+          float s0, s1;
+          add2(s0, s1, v[0], v[1], v[2], v[3]);
+          add2(s0, s1, s0, s1, v[4], v[5]);
+          add2(s0, s1, s0, s1, v[6], v[7]);
+          float sm = s0 + s1;
+          sm += __shfl_xor_sync(0xffffffffu, sm, 1);
+          sm += __shfl_xor_sync(0xffffffffu, sm, 2);
+          sm += __shfl_xor_sync(0xffffffffu, sm, 4);
+          const float nmu = sm * (-1.0f / 64);
+#pragma unroll
+          for (int k = 0; k < 8; k += 2) add2(v[k], v[k + 1], v[k], v[k + 1], nmu, nmu);
+          float q0s, q1s;
+          mul2(q0s, q1s, v[0], v[1], v[0], v[1]);
+#pragma unroll
+          for (int k = 2; k < 8; k += 2) fma2(q0s, q1s, v[k], v[k + 1], v[k], v[k + 1], q0s, q1s);
+          float sq = q0s + q1s;
+          sq += __shfl_xor_sync(0xffffffffu, sq, 1);
+          sq += __shfl_xor_sync(0xffffffffu, sq, 2);
+          sq += __shfl_xor_sync(0xffffffffu, sq, 4);
+          inv = rsqrtf(sq * (1.0f / 64) + p.eps);
+        }
+        // y_lo = inv * (A_lo d_lo + B_lo d_hi) + C_lo ; y_hi = inv * (A_hi d_hi + B_hi d_lo) + C_hi
+        float y[8];
+#pragma unroll
+        for (int k = 0; k < 4; k += 2) {
+          float t0, t1;
+          mul2(t0, t1, cB[k], cB[k + 1], v[4 + k], v[5 + k]);
+          fma2(t0, t1, cA[k], cA[k + 1], v[k], v[k + 1], t0, t1);
+          fma2(y[k], y[k + 1], t0, t1, inv, inv, cC[k], cC[k + 1]);
+          mul2(t0, t1, cB[4 + k], cB[5 + k], v[k], v[k + 1]);
+          fma2(t0, t1, cA[4 + k], cA[5 + k], v[4 + k], v[5 + k], t0, t1);
+          fma2(y[4 + k], y[5 + k], t0, t1, inv, inv, cC[4 + k], cC[5 + k]);
+        }
+        const uint32_t w0 = Elem<E>::pack2(y[0], y[1]), w1 = Elem<E>::pack2(y[2], y[3]);
+        const uint32_t w2 = Elem<E>::pack2(y[4], y[5]), w3 = Elem<E>::pack2(y[6], y[7]);
+        float n2 = 0.f;
+        if (tok_ok) {
+          E* row = out + (static_cast<uint64_t>(q0 + j) * a.t + tok) * 64;
+          *reinterpret_cast<uint2*>(row + 4 * g) = make_uint2(w0, w1);
+          *reinterpret_cast<uint2*>(row + 32 + 4 * g) = make_uint2(w2, w3);
+          if (p.norm2_max) {  // squared norm of the values as stored
+            const float2 r0 = Elem<E>::unpack2(w0), r1 = Elem<E>::unpack2(w1);
+            const float2 r2 = Elem<E>::unpack2(w2), r3 = Elem<E>::unpack2(w3);
+            float m0, m1;
+            mul2(m0, m1, r0.x, r0.y, r0.x, r0.y);
+            fma2(m0, m1, r1.x, r1.y, r1.x, r1.y, m0, m1);
+            fma2(m0, m1, r2.x, r2.y, r2.x, r2.y, m0, m1);
+            fma2(m0, m1, r3.x, r3.y, r3.x, r3.y, m0, m1);
+            n2 = m0 + m1;
+          }
+        }
+        if (p.norm2_max) {  // uniform branch: the row's 8 lanes add their parts
+          n2 += __shfl_xor_sync(0xffffffffu, n2, 1);
+          n2 += __shfl_xor_sync(0xffffffffu, n2, 2);
+          n2 += __shfl_xor_sync(0xffffffffu, n2, 4);
+          n2_run = fmaxf(n2_run, n2);
+        }
+      }
+    }
+    __syncthreads();  // every thread is done with stage st (or the block is aborting)
+    if (*reinterpret_cast<volatile int*>(abort_flag)) break;
+    if (threadIdx.x == 0 && issued < u_end) issue(issued++, st);
+  }
+
+  // Let every load thread 0 issued land before the block can exit (on the
+  // normal path all of them have been consumed already).
+  if (threadIdx.x == 0) {
+    int no_abort = 0;
+    for (uint64_t k = i; k < issued - u_begin; ++k)
+      mbar_wait(&full[k & 1], static_cast<uint32_t>(k >> 1) & 1u, &no_abort, a.status, kSitePrepFull, a.timeout_ns);
+  }
+  if (cur_job != 0xffffffffu) flush_norm(cur_job);
+}
+
 // One warp per row, any width; two-pass statistics like layernorm.wesl.
 template <typename T>
 __global__ void __launch_bounds__(256) layernorm_kernel(const T* __restrict__ x, T* __restrict__ out,
@@ -410,6 +659,42 @@ cudaError_t prep_dispatch_out(cudaStream_t stream, const PrepJobs& jobs, int n_j
     case kF16: qk_prep_kernel<In, __half><<<grid, 256, 0, stream>>>(jobs, sh, heads, t); break;
     default: qk_prep_kernel<In, float><<<grid, 256, 0, stream>>>(jobs, sh, heads, t); break;
   }
+  return cudaGetLastError();
+}
+
+// The TMA-staged prep, when every tensor of the launch can be described by a
+// tensor map (16-byte aligned, row strides multiples of 8 elements);
+// *launched stays false otherwise and the caller takes the register kernel.
+template <typename E>
+cudaError_t prep_tma(cudaStream_t stream, const PrepJobs& jobs, int n_jobs, uint32_t S, uint32_t H, uint32_t t,
+                     int* status, uint64_t timeout_ns, bool* launched) {
+  CUtensorMap maps[kMaxPrepJobs];
+  for (int i = 0; i < n_jobs; ++i) {
+    const PrepJob& j = jobs.job[i];
+    const RowLayout& l = j.lx;
+    if ((reinterpret_cast<uintptr_t>(j.x) & 15u) || (reinterpret_cast<uintptr_t>(j.out) & 15u) || (l.t & 7u) ||
+        (l.h & 7u) || (l.s & 7u))
+      return cudaSuccess;
+    if (!make_row_map(&maps[i], j.x, l, Elem<E>::kBf16, t, H, S, kTpTokens, nullptr)) return cudaSuccess;
+  }
+  for (int i = n_jobs; i < kMaxPrepJobs; ++i) maps[i] = maps[0];
+  TmaPrepArgs a{};
+  a.jobs = jobs;
+  a.sh = S * H;
+  a.heads = H;
+  a.t = t;
+  a.n_tb = (t + kTpTokens - 1) / kTpTokens;
+  a.n_sc = (a.sh + kTpSeqs - 1) / kTpSeqs;
+  a.units = static_cast<uint64_t>(n_jobs) * a.n_tb * a.n_sc;
+  a.status = status;
+  a.timeout_ns = timeout_ns;
+  const cudaError_t e =
+      ensure_dynamic_smem(reinterpret_cast<const void*>(qk_prep_tma_kernel<E>), static_cast<int>(kTpSmemBytes));
+  if (e != cudaSuccess) return e;
+  const uint64_t cap = static_cast<uint64_t>(kTpBlocksPerSm) * static_cast<uint64_t>(current_sm_count());
+  const unsigned grid = static_cast<unsigned>(a.units < cap ? a.units : cap);
+  qk_prep_tma_kernel<E><<<grid, kTpThreads, kTpSmemBytes, stream>>>(maps[0], maps[1], maps[2], a);
+  *launched = true;
   return cudaGetLastError();
 }
 
@@ -585,12 +870,19 @@ struct PermuteRun {
 }  // namespace
 
 cudaError_t launch_qk_prep(cudaStream_t stream, int in_code, int out_code, uint32_t S, uint32_t H, uint32_t t,
-                           const PrepJob* jobs, int n_jobs) {
+                           const PrepJob* jobs, int n_jobs, int* status, uint64_t timeout_ns) {
   const uint32_t sh = S * H;
   if (sh == 0 || t == 0 || n_jobs == 0) return cudaSuccess;
   if (n_jobs < 0 || n_jobs > kMaxPrepJobs) return cudaErrorInvalidValue;
   PrepJobs all{};
   for (int i = 0; i < n_jobs; ++i) all.job[i] = jobs[i];
+  if (in_code == out_code && in_code != kF32 && status) {
+    bool launched = false;
+    const cudaError_t e = in_code == kBF16
+                              ? prep_tma<__nv_bfloat16>(stream, all, n_jobs, S, H, t, status, timeout_ns, &launched)
+                              : prep_tma<__half>(stream, all, n_jobs, S, H, t, status, timeout_ns, &launched);
+    if (launched || e != cudaSuccess) return e;
+  }
   switch (in_code) {
     case kBF16: return prep_dispatch_out<__nv_bfloat16>(stream, all, n_jobs, out_code, sh, H, t);
     case kF16: return prep_dispatch_out<__half>(stream, all, n_jobs, out_code, sh, H, t);
@@ -599,9 +891,10 @@ cudaError_t launch_qk_prep(cudaStream_t stream, int in_code, int out_code, uint3
 }
 
 cudaError_t launch_qk_prep(cudaStream_t stream, const void* x, int in_code, const RowLayout& lx, void* out,
-                           int out_code, uint32_t S, uint32_t H, uint32_t t, const QkPrologue& p) {
+                           int out_code, uint32_t S, uint32_t H, uint32_t t, const QkPrologue& p, int* status,
+                           uint64_t timeout_ns) {
   PrepJob job{x, lx, out, p};
-  return launch_qk_prep(stream, in_code, out_code, S, H, t, &job, 1);
+  return launch_qk_prep(stream, in_code, out_code, S, H, t, &job, 1, status, timeout_ns);
 }
 
 cudaError_t launch_layernorm(cudaStream_t stream, const void* x, void* out, int code, const float* w, const float* b,

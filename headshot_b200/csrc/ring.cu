@@ -338,7 +338,7 @@ hs_status ring_attention(hs_ring* ring, const void* q, const void* k, const void
     const hs::PrepJob jobs[2] = {{k, in_rows, b0, kp}, {q, in_rows, ring->state, qp}};
     {
       hs::ProfScope prof(ctx, st, "qk_prep");
-      e = hs::launch_qk_prep(st, code, code, 1, H, tr, jobs, 2);
+      e = hs::launch_qk_prep(st, code, code, 1, H, tr, jobs, 2, ctx->d_status, hs::ctx_timeout_ns(ctx));
     }
     if (e != cudaSuccess) return hs::abi_cuda_fail(e, "ring Q'/K' prep");
     q_use = ring->state;
