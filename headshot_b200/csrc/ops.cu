@@ -347,9 +347,14 @@ __global__ void __launch_bounds__(kTpThreads, kTpBlocksPerSm)
   }
   __syncthreads();
 
+  // Tensor of unit u (units are tensor-major, at most kMaxPrepJobs tensors):
+  // two compares instead of a 64-bit division.
+  auto job_of = [&](uint64_t u) {
+    return static_cast<uint32_t>(u >= per_job) + static_cast<uint32_t>(u >= 2ull * per_job);
+  };
   // Thread 0: the TMA loads of unit u into stage `st`.
   auto issue = [&](uint64_t u, int st) {
-    const uint32_t job = static_cast<uint32_t>(u / per_job);
+    const uint32_t job = job_of(u);
     const uint32_t rem = static_cast<uint32_t>(u - static_cast<uint64_t>(job) * per_job);
     const uint32_t tb = rem / a.n_sc;
     const uint32_t q0 = (rem - tb * a.n_sc) * kTpSeqs;
@@ -389,7 +394,7 @@ __global__ void __launch_bounds__(kTpThreads, kTpBlocksPerSm)
   uint64_t i = 0;
   for (uint64_t u = u_begin; u < u_end; ++u, ++i) {
     const int st = static_cast<int>(i & 1);
-    const uint32_t job = static_cast<uint32_t>(u / per_job);
+    const uint32_t job = job_of(u);
     const uint32_t rem = static_cast<uint32_t>(u - static_cast<uint64_t>(job) * per_job);
     const uint32_t tb = rem / a.n_sc;
     const uint32_t q0 = (rem - tb * a.n_sc) * kTpSeqs;
@@ -429,7 +434,10 @@ __global__ void __launch_bounds__(kTpThreads, kTpBlocksPerSm)
         cC[4 + k] = b_hi * cs_hi + b_lo * sn_hi;
       }
     }
-    const QkPrologue& p = job_p->p;
+    // The tensor's flags, read once per unit rather than per row.
+    const bool do_ln = job_p->p.ln != 0;
+    const bool do_norm = job_p->p.norm2_max != nullptr;
+    const float eps = job_p->p.eps;
     E* __restrict__ out = static_cast<E*>(job_p->out);
 
     const bool ok = mbar_wait(&full[st], static_cast<uint32_t>(i >> 1) & 1u, abort_flag, a.status, kSitePrepFull,
@@ -449,7 +457,7 @@ __global__ void __launch_bounds__(kTpThreads, kTpBlocksPerSm)
           v[4] = f2.x; v[5] = f2.y; v[6] = f3.x; v[7] = f3.y;
         }
         float inv = 1.f;
-        if (p.ln) {
+        if (do_ln) {
           float s0, s1;
           add2(s0, s1, v[0], v[1], v[2], v[3]);
           add2(s0, s1, s0, s1, v[4], v[5]);
@@ -469,7 +477,7 @@ __global__ void __launch_bounds__(kTpThreads, kTpBlocksPerSm)
           sq += __shfl_xor_sync(0xffffffffu, sq, 1);
           sq += __shfl_xor_sync(0xffffffffu, sq, 2);
           sq += __shfl_xor_sync(0xffffffffu, sq, 4);
-          inv = rsqrtf(sq * (1.0f / 64) + p.eps);
+          inv = rsqrtf(sq * (1.0f / 64) + eps);
         }
         // y_lo = inv * (A_lo d_lo + B_lo d_hi) + C_lo ; y_hi = inv * (A_hi d_hi + B_hi d_lo) + C_hi
         float y[8];
@@ -490,7 +498,7 @@ __global__ void __launch_bounds__(kTpThreads, kTpBlocksPerSm)
           E* row = out + (static_cast<uint64_t>(q0 + j) * a.t + tok) * 64;
           *reinterpret_cast<uint2*>(row + 4 * g) = make_uint2(w0, w1);
           *reinterpret_cast<uint2*>(row + 32 + 4 * g) = make_uint2(w2, w3);
-          if (p.norm2_max) {  // squared norm of the values as stored
+          if (do_norm) {  // squared norm of the values as stored
             const float2 r0 = Elem<E>::unpack2(w0), r1 = Elem<E>::unpack2(w1);
             const float2 r2 = Elem<E>::unpack2(w2), r3 = Elem<E>::unpack2(w3);
             float m0, m1;
@@ -501,7 +509,7 @@ __global__ void __launch_bounds__(kTpThreads, kTpBlocksPerSm)
             n2 = m0 + m1;
           }
         }
-        if (p.norm2_max) {  // uniform branch: the row's 8 lanes add their parts
+        if (do_norm) {  // uniform branch: the row's 8 lanes add their parts
           n2 += __shfl_xor_sync(0xffffffffu, n2, 1);
           n2 += __shfl_xor_sync(0xffffffffu, n2, 2);
           n2 += __shfl_xor_sync(0xffffffffu, n2, 4);
