@@ -280,10 +280,12 @@ __global__ void __launch_bounds__(256) qk_prep_kernel(PrepJobs jobs, uint32_t sh
 // Work unit = 32 consecutive tokens of 8 sequences of one tensor.  A block
 // takes a contiguous range of units (sequences fastest, so a thread's folded
 // table constants, which depend on the token only, are rebuilt only when the
-// token block changes) and streams them through two shared-memory stages:
-// one thread issues the 8 TMA box loads (32 rows x 128 B each) of unit i+2
-// into the stage unit i has just released, so HBM reads stay in flight while
-// the block computes.  Thread (token, g) computes elements [4g, 4g+4) and
+// token block changes) and streams them through two shared-memory stages.
+// A ninth warp is the producer: its lane 0 issues the 8 TMA box loads (32
+// rows x 128 B each) of unit i+2 into the stage unit i used as soon as all
+// eight compute warps have released it (one arrival per warp on the stage's
+// `empty` barrier), so HBM reads stay in flight while the block computes and
+// the compute warps never wait for one another.  Thread (token, g) computes elements [4g, 4g+4) and
 // their rotate-half partners [32+4g, 36+4g) of its token's row in each
 // sequence of the unit.  LayerNorm's affine and the RoPE rotation fold into
 // three constants per output element (d = x - mean, inv = 1/sqrt(var + eps)):
@@ -297,7 +299,9 @@ constexpr int kTpSeqs = 8;
 constexpr int kTpStages = 2;
 constexpr uint32_t kTpBoxBytes = kTpTokens * 128;            // 32 rows of 64 16-bit elements
 constexpr uint32_t kTpStageBytes = kTpSeqs * kTpBoxBytes;    // 32 KiB
-constexpr int kTpThreads = kTpTokens * 8;
+constexpr int kTpThreads = kTpTokens * 8;           // compute threads (8 per 64-wide row)
+constexpr int kTpComputeWarps = kTpThreads / 32;
+constexpr int kTpBlockThreads = kTpThreads + 32;     // + the producer warp
 constexpr int kTpBlocksPerSm = 3;
 constexpr size_t kTpSmemBytes = 1024 /*alignment slack*/ + kTpStages * kTpStageBytes + 64;
 constexpr int kSitePrepFull = 0x201;
@@ -315,13 +319,14 @@ struct TmaPrepArgs {
 };
 
 template <typename E>
-__global__ void __launch_bounds__(kTpThreads, kTpBlocksPerSm)
+__global__ void __launch_bounds__(kTpBlockThreads, kTpBlocksPerSm)
     qk_prep_tma_kernel(const __grid_constant__ CUtensorMap tm0, const __grid_constant__ CUtensorMap tm1,
                        const __grid_constant__ CUtensorMap tm2, const __grid_constant__ TmaPrepArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* stages = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(stages + kTpStages * kTpStageBytes);
-  int* abort_flag = reinterpret_cast<int*>(full + kTpStages);
+  uint64_t* full = reinterpret_cast<uint64_t*>(stages + kTpStages * kTpStageBytes);  // unit landed
+  uint64_t* empty = full + kTpStages;  // every compute warp is done with the stage
+  int* abort_flag = reinterpret_cast<int*>(empty + kTpStages);
 
   const uint64_t u_begin = blockIdx.x * a.units / gridDim.x;
   const uint64_t u_end = (blockIdx.x + 1ull) * a.units / gridDim.x;
@@ -341,7 +346,10 @@ __global__ void __launch_bounds__(kTpThreads, kTpBlocksPerSm)
       static_cast<uint32_t>(lt) * 128 + ((static_cast<uint32_t>(4 + (g >> 1)) ^ sw) << 4) + (g & 1) * 8;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kTpStages; ++s) mbar_init(&full[s], 1);
+    for (int s = 0; s < kTpStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kTpComputeWarps);
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -352,7 +360,7 @@ __global__ void __launch_bounds__(kTpThreads, kTpBlocksPerSm)
   auto job_of = [&](uint64_t u) {
     return static_cast<uint32_t>(u >= per_job) + static_cast<uint32_t>(u >= 2ull * per_job);
   };
-  // Thread 0: the TMA loads of unit u into stage `st`.
+  // The producer lane: the TMA loads of unit u into stage `st`.
   auto issue = [&](uint64_t u, int st) {
     const uint32_t job = job_of(u);
     const uint32_t rem = static_cast<uint32_t>(u - static_cast<uint64_t>(job) * per_job);
@@ -367,9 +375,24 @@ __global__ void __launch_bounds__(kTpThreads, kTpBlocksPerSm)
                   static_cast<int>(tb * kTpTokens), static_cast<int>(q % a.heads), static_cast<int>(q / a.heads));
     }
   };
-  uint64_t issued = u_begin;
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < kTpStages && issued < u_end; ++s) issue(issued++, s);
+  if (warp == kTpComputeWarps) {
+    if (lane == 0) {
+      uint64_t n = 0;  // units issued
+      for (uint64_t u = u_begin; u < u_end; ++u, ++n) {
+        const int st = static_cast<int>(n % kTpStages);
+        if (n >= kTpStages && !mbar_wait(&empty[st], static_cast<uint32_t>(n / kTpStages - 1) & 1u, abort_flag,
+                                         a.status, kSitePrepFull, a.timeout_ns))
+          break;
+        issue(u, st);
+      }
+      // Let the last loads land before the block can exit (on the normal path
+      // the compute warps have consumed them already).
+      int no_abort = 0;
+      for (uint64_t k = n > kTpStages ? n - kTpStages : 0; k < n; ++k)
+        mbar_wait(&full[k % kTpStages], static_cast<uint32_t>(k / kTpStages) & 1u, &no_abort, a.status,
+                  kSitePrepFull, a.timeout_ns);
+    }
+    return;
   }
 
   float cA[8], cB[8], cC[8];  // [0..3] lower-half outputs, [4..7] upper-half outputs
@@ -393,7 +416,7 @@ __global__ void __launch_bounds__(kTpThreads, kTpBlocksPerSm)
 
   uint64_t i = 0;
   for (uint64_t u = u_begin; u < u_end; ++u, ++i) {
-    const int st = static_cast<int>(i & 1);
+    const int st = static_cast<int>(i % kTpStages);
     const uint32_t job = job_of(u);
     const uint32_t rem = static_cast<uint32_t>(u - static_cast<uint64_t>(job) * per_job);
     const uint32_t tb = rem / a.n_sc;
@@ -440,7 +463,7 @@ __global__ void __launch_bounds__(kTpThreads, kTpBlocksPerSm)
     const float eps = job_p->p.eps;
     E* __restrict__ out = static_cast<E*>(job_p->out);
 
-    const bool ok = mbar_wait(&full[st], static_cast<uint32_t>(i >> 1) & 1u, abort_flag, a.status, kSitePrepFull,
+    const bool ok = mbar_wait(&full[st], static_cast<uint32_t>(i / kTpStages) & 1u, abort_flag, a.status, kSitePrepFull,
                               a.timeout_ns);
     if (ok) {
       const uint8_t* box0 = stages + st * kTpStageBytes;
@@ -517,18 +540,11 @@ __global__ void __launch_bounds__(kTpThreads, kTpBlocksPerSm)
         }
       }
     }
-    __syncthreads();  // every thread is done with stage st (or the block is aborting)
-    if (*reinterpret_cast<volatile int*>(abort_flag)) break;
-    if (threadIdx.x == 0 && issued < u_end) issue(issued++, st);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);  // this warp is done with stage st
+    if (__any_sync(0xffffffffu, !ok || *reinterpret_cast<volatile int*>(abort_flag) != 0)) break;
   }
 
-  // Let every load thread 0 issued land before the block can exit (on the
-  // normal path all of them have been consumed already).
-  if (threadIdx.x == 0) {
-    int no_abort = 0;
-    for (uint64_t k = i; k < issued - u_begin; ++k)
-      mbar_wait(&full[k & 1], static_cast<uint32_t>(k >> 1) & 1u, &no_abort, a.status, kSitePrepFull, a.timeout_ns);
-  }
   if (cur_job != 0xffffffffu) flush_norm(cur_job);
 }
 
@@ -701,7 +717,7 @@ cudaError_t prep_tma(cudaStream_t stream, const PrepJobs& jobs, int n_jobs, uint
   if (e != cudaSuccess) return e;
   const uint64_t cap = static_cast<uint64_t>(kTpBlocksPerSm) * static_cast<uint64_t>(current_sm_count());
   const unsigned grid = static_cast<unsigned>(a.units < cap ? a.units : cap);
-  qk_prep_tma_kernel<E><<<grid, kTpThreads, kTpSmemBytes, stream>>>(maps[0], maps[1], maps[2], a);
+  qk_prep_tma_kernel<E><<<grid, kTpBlockThreads, kTpSmemBytes, stream>>>(maps[0], maps[1], maps[2], a);
   *launched = true;
   return cudaGetLastError();
 }
