@@ -185,6 +185,16 @@ def test_fused_f32_storage(gpu_ctx):
     gate(ours, ref)
 
 
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+@pytest.mark.parametrize("s,h,t", [(3, 3, 32), (1, 9, 31), (2, 5, 65), (17, 1, 96)])
+def test_fused_prep_unit_edges(gpu_ctx, dtype, s, h, t):
+    # The QK prep moves 32 tokens of 8 sequences per unit through shared
+    # memory: sequence counts just past a multiple of 8, and token counts at,
+    # below and above the 32-token unit, leave partial units both ways.
+    ours, ref = _fused_case(gpu_ctx, s, h, t, dtype, prefix=5, tpf=t, grid=(37, 37), seed=40 + s * h + t)
+    gate(ours, ref)
+
+
 # ---- companion ops -----------------------------------------------------------
 
 @pytest.mark.parametrize("dtype", ["f32", "f16", "bf16"])
@@ -257,6 +267,25 @@ def test_block_fused_matches_oracle(gpu_ctx, dtype, s, t, tpf):
                                   rope=Rope(c(sin), c(cos), prefix, tpf))
     gpu_ctx.sync()
     assert out.shape == (s * t, h * d)
+    gate(host(out), ref)
+
+
+@pytest.mark.parametrize("dtype,s,h,t", [("bf16", 3, 3, 33), ("f16", 1, 9, 95)])
+def test_block_fused_prep_unit_edges(gpu_ctx, dtype, s, h, t):
+    # The prep's partial units on the token-major projection layout (row
+    # stride H*64, so the tensor map steps heads by one 128-byte row).
+    d, prefix, eps = 64, 5, 1e-6
+    qt, kt, vt, (qw, qb, kw, kb) = _block_inputs(s, h, t, dtype, 71 + t)
+    sin, cos = oracle.rope_tables(37, 37)
+    q, k, v = (oracle.split_heads(x, s, t, h, d) for x in (qt, kt, vt))
+    qn = rounded(oracle.qk_prep(q, qw, qb, eps, sin, cos, prefix, t), dtype)
+    kn = rounded(oracle.qk_prep(k, kw, kb, eps, sin, cos, prefix, t), dtype)
+    ref = oracle.attn_merge(oracle.attention(qn, kn, v))
+    c = lambda a: torch.from_numpy(a).cuda()  # noqa: E731
+    out = gpu_ctx.attention_block(dev(qt, dtype), dev(kt, dtype), dev(vt, dtype), s, t, h,
+                                  qk_norm=QkNorm(c(qw), c(qb), c(kw), c(kb), eps),
+                                  rope=Rope(c(sin), c(cos), prefix, t))
+    gpu_ctx.sync()
     gate(host(out), ref)
 
 
