@@ -42,6 +42,16 @@ WORKLOADS = {
     "frame": dict(S=200, H=16, frames=1, T_f=1374, dtype="f16", seed=2, prefix=5, grid=(37, 37), eps=1e-6,
                   name="batched frame attention, 200 frames x 1374 tokens, 16 heads x 64, fp16, "
                        "fused QK-LayerNorm + 2D RoPE (37x37, 5 special tokens)"),
+    # The same two workloads with a QK-norm gain that lifts the score bound past the
+    # fixed-offset limit (bf16 48, f16 14), so the kernel runs its running-max softmax.
+    "global_running_max": dict(S=1, H=16, frames=200, T_f=1374, dtype="bf16", seed=3, prefix=5, grid=(37, 37),
+                               eps=1e-6, ln_gain=2.5,
+                               name="config 4 with QK-LayerNorm weight 2.5 (score bound ~72 > 48): the "
+                                    "running-max softmax, 274,800 tokens, 16 heads x 64, bf16"),
+    "frame_running_max": dict(S=200, H=16, frames=1, T_f=1374, dtype="f16", seed=2, prefix=5, grid=(37, 37),
+                              eps=1e-6, ln_gain=1.2,
+                              name="config 3 with QK-LayerNorm weight 1.2 (score bound ~16.6 > 14): the "
+                                   "running-max softmax, 200 frames x 1374 tokens, 16 heads x 64, fp16"),
     # Same work as "frame" on the layout Block::forward hands over: q, k, v are the
     # (S*T, H*D) projection outputs and the output is the merged (S*T, H*D) tensor
     # (split_heads, QK-norm, RoPE, attention and attn_merge in one call).
@@ -60,13 +70,28 @@ WORKLOADS = {
     # pairs + the 4 head-input caches) over 100 frames of 518x518 RGB, bf16, random weights.
     "aggregator": dict(kind="aggregator", frames=100, size=518, dtype="bf16", seed=4,
                        name="VGGT-1B aggregator forward, 100 frames 518x518 (patch 14, 37x37, 5 prefix tokens), "
-                            "bf16, random-init N(0,0.02), LayerScale 1e-5"),
+                            "DINO 24 layers + 24 frame/global block pairs, bf16, random-init N(0,0.02), "
+                            "LayerScale 1e-5"),
+    # The reference server's own trunk layout (headshot-shared src/model.rs:25): five of the
+    # 24 inter-frame layers attend over the 5 prefix tokens of every frame only.
+    "aggregator_shared": dict(kind="aggregator", layout="headshot_shared", frames=100, size=518, dtype="bf16",
+                              seed=4,
+                              name="VGGT aggregator forward in headshot-server's trunk layout (19 global + 5 "
+                                   "register-only inter-frame layers), 100 frames 518x518, bf16, random-init"),
     # BASELINE config 1's shape: one frame block + one global block over 4 frames x 1374 tokens,
     # dim 1024, random weights N(0,0.02), LayerScale 1e-5, QK-LN eps 1e-6, seed 0 (the reference
     # runs it f32 on lavapipe; here bf16 storage, the tensor-core path).
     "block_pair": dict(kind="block_pair", frames=4, t=1374, dtype="bf16", seed=0,
-                       name="VGGT block pair (frame block + global block), 4 frames x 1374 tokens, dim 1024, "
-                            "16 heads x 64, MLP 4096, bf16, random-init N(0,0.02), LayerScale 1e-5"),
+                       name="config 1's shape in bf16 storage (not config 1's f32): VGGT block pair (frame block + "
+                            "global block), 4 frames x 1374 tokens, dim 1024, 16 heads x 64, MLP 4096, "
+                            "random-init N(0,0.02), LayerScale 1e-5"),
+    # Config 1 as BASELINE words it, f32 storage throughout: f32 LayerNorms and linears (f32
+    # arithmetic on the CUDA cores), f32 q/k/v into the attention, whose tensor-core products
+    # take bf16-rounded operands (f32 softmax statistics, f32 output).
+    "block_pair_f32": dict(kind="block_pair", frames=4, t=1374, dtype="f32", seed=0,
+                           name="BASELINE config 1: VGGT block pair (frame block + global block), 4 frames x 1374 "
+                                "tokens, dim 1024, 16 heads x 64, MLP 4096, f32 storage (attention operands "
+                                "rounded to bf16 for the tensor core), random-init N(0,0.02), LayerScale 1e-5"),
     "frame_block": dict(S=200, H=16, frames=1, T_f=1374, dtype="f16", seed=2, prefix=5, grid=(37, 37), eps=1e-6,
                         layout="block",
                         name="batched frame attention on the projection layout (S*T, H*D) in and merged out, "
@@ -74,8 +99,34 @@ WORKLOADS = {
 }
 
 
-# DRAM bytes (read + write) per attention launch, one-pass ncu captures.
-MEASURED_TRAFFIC = {"global": 12.26e9 + 574.90e6, "global43k": 270.41e6 + 75.09e6}
+# DRAM bytes (read + write) per attention launch from one-pass ncu captures
+# (dram__bytes_read.sum + dram__bytes_write.sum), each stored with the sha256 of
+# the attention kernel's sources at capture time: a figure whose hash no longer
+# matches the sources is not reported (traffic null, with the reason).
+MEASURED_TRAFFIC = {
+    "global": {"bytes": 12.26e9 + 574.90e6, "sources_sha256": None},
+    "global43k": {"bytes": 270.41e6 + 75.09e6, "sources_sha256": None},
+}
+TRAFFIC_SOURCES = ("headshot_b200/csrc/attention_sm100.cu", "headshot_b200/csrc/hs_ptx.cuh")
+
+
+def attention_sources_sha256() -> str:
+    import hashlib
+
+    h = hashlib.sha256()
+    for rel in TRAFFIC_SOURCES:
+        h.update((ROOT / rel).read_bytes())
+    return h.hexdigest()
+
+
+def measured_traffic(workload: str) -> tuple[int | None, str]:
+    """(bytes per launch, source note) for `workload`, or (None, why not)."""
+    rec = MEASURED_TRAFFIC.get(workload)
+    if rec is None:
+        return None, "not captured for this workload"
+    if rec["sources_sha256"] != attention_sources_sha256():
+        return None, "stale: the attention kernel's sources changed since the ncu capture"
+    return int(rec["bytes"]), "ncu dram__bytes_read+write of this launch (1 pass), kernel sources unchanged"
 
 
 def log(*a):
@@ -161,7 +212,7 @@ def cpu_attention_sample(q_h, k_h, v_h, T, seconds_target: float, threads: int, 
     import oracle
 
     sin, cos = oracle.rope_tables(*prep["grid"])
-    w = np.ones(64, np.float32)
+    w = np.full(64, prep.get("ln_gain", 1.0), np.float32)
     b = np.zeros(64, np.float32)
     qn = oracle.qk_prep(q_h, w, b, prep["eps"], sin, cos, prep["prefix"], prep["T_f"])
     kn = oracle.qk_prep(k_h, w, b, prep["eps"], sin, cos, prep["prefix"], prep["T_f"])
@@ -247,7 +298,7 @@ def run_ours(args, wl: dict, rank: int, world: int, local: int) -> dict | None:
 
     sin, cos = rope_mod.tables(None, *wl["grid"])
     sin_d, cos_d = torch.from_numpy(sin).to(dev), torch.from_numpy(cos).to(dev)
-    w = torch.ones(64, device=dev)
+    w = torch.full((64,), float(wl.get("ln_gain", 1.0)), device=dev)
     b = torch.zeros(64, device=dev)
     norm = QkNorm(w, b, w, b, wl["eps"])
 
@@ -412,22 +463,22 @@ def run_ours(args, wl: dict, rank: int, world: int, local: int) -> dict | None:
     attn_per_launch_ms = attn_ms / max(attn_n, 1)
     flops_per_launch = flops_rank if session is None else flops_rank / world
     achieved = flops_per_launch / (attn_per_launch_ms / 1e3) / 1e12
-    # DRAM bytes per attention launch from one-pass ncu captures of these
-    # exact single-GPU launches (dram__bytes_read.sum + dram__bytes_write.sum;
-    # profiles/attn_fwd_sm100_dram_traffic.md).  Not captured for the other
-    # workloads or for ring steps: null there.
-    traffic = None
-    if world == 1 and args.workload in MEASURED_TRAFFIC:
-        traffic = int(MEASURED_TRAFFIC[args.workload])
+    # DRAM bytes per attention launch from one-pass ncu captures of these exact
+    # single-GPU launches, reported only while the kernel sources still hash to
+    # the captured ones; ring steps and uncaptured workloads report null.
+    traffic, traffic_note = measured_traffic(args.workload) if world == 1 else (None, "not captured for ring steps")
     roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peaks["bf16"], "unit": "TFLOP/s",
                 "frac": round(achieved / peaks["bf16"], 4), "traffic": traffic,
-                "traffic_source": "ncu dram__bytes_read+write of this launch (1 pass)" if traffic else None,
+                "traffic_source": traffic_note,
                 "peak_source": f"{peaks['source']} bf16 burst (MEASURED_PEAKS.json)",
                 # the launches run back to back for seconds under the 1000 W cap, the regime of
                 # the sustained figure: both fractions are given, `frac` is the burst one
                 "frac_of_sustained_peak": round(achieved / peaks["bf16_sustained"], 4),
                 "kernel": "attn_fwd_sm100", "kernel_ms_per_launch": round(attn_per_launch_ms, 3),
-                "launches": attn_n, "kernel_share_of_step": round(attn_ms / max(all_ms, 1e-9), 4)}
+                "launches": attn_n,
+                # device time of this rank's attention launches over the timed region's device time
+                "kernel_share_of_step": round(attn_ms / max(ms_local, 1e-9), 4),
+                "other_launches_ms_per_step": round((all_ms - attn_ms) / args.steps, 3)}
 
     result = None
     if rank == 0:
@@ -696,7 +747,7 @@ def run_aggregator(args, wl: dict, rank: int, world: int, local: int) -> dict | 
     from headshot_b200.session import RingSession, shard_bounds
 
     tdt = {"bf16": torch.bfloat16, "f16": torch.float16}[wl["dtype"]]
-    cfg = AggregatorConfig()
+    cfg = _aggregator_config(wl)
     ctx = GpuContext(local)
     dev = torch.device("cuda", local)
     n_total, size = wl["frames"], wl["size"]
@@ -742,6 +793,13 @@ def run_aggregator(args, wl: dict, rank: int, world: int, local: int) -> dict | 
     att_ms, att_n = ctx.prof_read("attention")
     lin_ms, lin_n = ctx.prof_read("linear")
     all_ms, all_n = ctx.prof_read("*")
+    # device time per kind of launch over this rank's timed region
+    local_ms = e0.elapsed_time(e1)
+    shares = {}
+    for kind in ("attention", "linear", "qk_prep", "layernorm", "cache_build", "copy_rows", "im2col_patch"):
+        k_ms, k_n = ctx.prof_read(kind)
+        shares[kind] = {"share_of_step": round(k_ms / local_ms, 4), "launches_per_step": round(k_n / args.steps, 1)}
+    shares["unbracketed"] = {"share_of_step": round(max(0.0, 1.0 - all_ms / local_ms), 4)}
     value = n_total / (ms / 1e3)
 
     # end to end: the rank's images up from pinned host memory, its four caches down; each
@@ -811,9 +869,10 @@ def run_aggregator(args, wl: dict, rank: int, world: int, local: int) -> dict | 
                          "peak_source": f"{peaks['source']} bf16 sustained (MEASURED_PEAKS.json): kernels inside a "
                                         f"seconds-long step",
                          "kernel": "attn_fwd_sm100 (all attention launches of the step)",
-                         "attention_share_of_step": round(att_ms / args.steps / ms, 3),
+                         "attention_share_of_step": round(att_ms / local_ms, 4),
                          "linear_tflops": round(lin_achieved, 1),
-                         "linear_share_of_step": round(lin_ms / args.steps / ms, 3)},
+                         "linear_share_of_step": round(lin_ms / local_ms, 4),
+                         "shares_by_kind": shares},
             "cpu_baseline": cpu,
             "e2e": {"value": round(n_total / (e2e_ms / 1e3), 3), "unit": "frames/s",
                     "h2d_bytes_per_step": images.numel() * 4 * world,
@@ -823,6 +882,12 @@ def run_aggregator(args, wl: dict, rank: int, world: int, local: int) -> dict | 
         }
     ctx.close()
     return result
+
+
+def _aggregator_config(wl: dict):
+    from headshot_b200.aggregator import AggregatorConfig
+
+    return AggregatorConfig.headshot_shared() if wl.get("layout") == "headshot_shared" else AggregatorConfig()
 
 
 def _block_pair_setup(wl: dict, dev, tdt):
@@ -856,7 +921,7 @@ def run_block_pair(args, wl: dict, rank: int, world: int, local: int) -> dict | 
 
     from headshot_b200.engine import GpuContext
 
-    tdt = {"bf16": torch.bfloat16, "f16": torch.float16}[wl["dtype"]]
+    tdt = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}[wl["dtype"]]
     ctx = GpuContext(local)
     dev = torch.device("cuda", local)
     cfg, fb, gb, x, rope = _block_pair_setup(wl, dev, tdt)
@@ -880,6 +945,8 @@ def run_block_pair(args, wl: dict, rank: int, world: int, local: int) -> dict | 
     torch.cuda.synchronize(dev)
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ctx.prof_reset()
+    ctx.prof_enable(True)
     for i in range(args.steps):
         flush.fill_(i & 0xFF)
         starts[i].record(stream)
@@ -887,7 +954,9 @@ def run_block_pair(args, wl: dict, rank: int, world: int, local: int) -> dict | 
         ends[i].record(stream)
     torch.cuda.synchronize(dev)
     barrier(world)
+    ctx.prof_enable(False)
     clocks = sampler.stop()
+    _, launches = ctx.prof_read("*")
     ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in zip(starts, ends)), world) / args.steps
     value = fl * world / (ms / 1e3) / 1e12
 
@@ -917,7 +986,9 @@ def run_block_pair(args, wl: dict, rank: int, world: int, local: int) -> dict | 
                    "kind": "port", "sample": f"one frame of the frame block and the global block's rows of that frame "
                                              f"(all 5496 keys), f32 oracle, {dt:.1f} s"}
         result = {
-            "metric": "block pair TFLOP/s (BASELINE config 1 shape: frame block + global block, 4 frames)",
+            "metric": ("block pair TFLOP/s (BASELINE config 1: frame block + global block, 4 frames, f32)"
+                       if wl["dtype"] == "f32" else
+                       "block pair TFLOP/s (BASELINE config 1's shape in bf16: frame block + global block, 4 frames)"),
             "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": wl["dtype"], "data": f"synthetic x N(0,1), random-init weights N(0,0.02), seed {wl['seed']}",
@@ -927,12 +998,13 @@ def run_block_pair(args, wl: dict, rank: int, world: int, local: int) -> dict | 
             "roofline": {"bound": "tensor", "achieved": round(fl / (ms / 1e3) / 1e12, 1), "peak": peaks["bf16"],
                          "unit": "TFLOP/s", "frac": round(fl / (ms / 1e3) / 1e12 / peaks["bf16"], 4),
                          "traffic": None, "peak_source": f"{peaks['source']} bf16 burst (MEASURED_PEAKS.json)",
-                         "kernel": "whole step (14 launches: attention, linears, LayerNorms, QK prep)"},
+                         "kernel": f"whole step ({launches // args.steps} launches: attention, linears, "
+                                   f"LayerNorms, QK prep)"},
             "cpu_baseline": cpu,
             "e2e": {"value": round(fl * world / (e2e_ms / 1e3) / 1e12, 2), "unit": "TFLOP/s",
                     "h2d_bytes_per_step": x.numel() * x.element_size() * world,
                     "d2h_bytes_per_step": out.numel() * out.element_size() * world, "ms_per_step": round(e2e_ms, 4)},
-            "gpu_launches": 14 * args.steps * world,
+            "gpu_launches": int(launches) * world,
             "clocks": clocks,
         }
     ctx.close()
@@ -1090,7 +1162,7 @@ def run_reference(args, wl: dict) -> dict:
     rng = np.random.default_rng(wl["seed"])
     q, k, v = (oracle.round_to(wl["dtype"], rng.standard_normal((1, 1, T, 64), np.float32)) for _ in range(3))
     sin, cos = oracle.rope_tables(*wl["grid"])
-    w = np.ones(64, np.float32)
+    w = np.full(64, wl.get("ln_gain", 1.0), np.float32)
     b = np.zeros(64, np.float32)
     # probe to size a step at ~ args.ref_step_seconds of CPU time
     qn = oracle.qk_prep(q, w, b, wl["eps"], sin, cos, wl["prefix"], T_f)
@@ -1166,9 +1238,7 @@ def run_reference_mlp(args, wl: dict) -> dict:
 def run_reference_aggregator(args, wl: dict) -> dict:
     """Config 5 on the CPU: the oracle's linear and attention rates, extrapolated to one
     forward (cpu_aggregator_estimate); each step re-measures the two samples."""
-    from headshot_b200.aggregator import AggregatorConfig
-
-    cfg = AggregatorConfig()
+    cfg = _aggregator_config(wl)
     threads = args.cpu_threads or _threads()
     for _ in range(args.warmup):
         cpu_aggregator_estimate(cfg, wl["frames"], wl["size"], threads, wl["dtype"], seconds=2.0)
@@ -1199,7 +1269,7 @@ def run_reference_block_pair(args, wl: dict) -> dict:
 
     threads = args.cpu_threads or _threads()
     cfg = AggregatorConfig()
-    tdt = {"bf16": torch.bfloat16, "f16": torch.float16}[wl["dtype"]]
+    tdt = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}[wl["dtype"]]
     g = torch.Generator().manual_seed(wl["seed"])  # CPU generator: the same shapes and distribution
     fb = Block(BlockWeights.random(cfg, True, tdt, g, torch.device("cpu")), cfg.heads, cfg.norm_eps)
     gb = Block(BlockWeights.random(cfg, True, tdt, g, torch.device("cpu")), cfg.heads, cfg.norm_eps)
@@ -1213,8 +1283,10 @@ def run_reference_block_pair(args, wl: dict) -> dict:
         fl += f
         dt += d
     value = fl / dt / 1e12
-    return {"impl": "reference", "metric": "block pair TFLOP/s (BASELINE config 1 shape: frame block + global "
-            "block, 4 frames)", "value": round(value, 6), "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
+    metric = ("block pair TFLOP/s (BASELINE config 1: frame block + global block, 4 frames, f32)"
+              if wl["dtype"] == "f32" else
+              "block pair TFLOP/s (BASELINE config 1's shape in bf16: frame block + global block, 4 frames)")
+    return {"impl": "reference", "metric": metric, "value": round(value, 6), "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 1), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": f"synthetic, rounded to {wl['dtype']}",
             "config": {"workload": wl["name"]},

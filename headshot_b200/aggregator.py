@@ -57,8 +57,12 @@ class Cancelled(RuntimeError):
 @dataclass(frozen=True)
 class AggregatorConfig:
     """Architecture of one aggregator.  The defaults are BASELINE config 5 (VGGT-1B at
-    518x518: patch 14 -> 37x37 patches, 1 camera + 4 register tokens per frame); the
-    reference checkpoint's own layout is patch 16, DINO prefix 5, trunk prefix 17."""
+    518x518: patch 14 -> 37x37 patches, 1 camera + 4 register tokens per frame, 24
+    frame-attention / global-attention block pairs, no register-only layers).
+    `headshot_shared()` is the reference server's own trunk layout: five of the 24
+    inter-frame layers attend over the prefix tokens only (headshot-shared
+    src/model.rs:25, trunk.rs:105-122).  The reference checkpoint's own token layout is
+    patch 16, DINO prefix 5, trunk prefix 17."""
 
     dim: int = 1024
     heads: int = 16
@@ -68,12 +72,18 @@ class AggregatorConfig:
     dino_prefix: int = 5  # cls + storage tokens (dino.rs:11)
     trunk_pairs: int = 24
     trunk_prefix: int = 5  # camera + register tokens (trunk.rs:15)
-    register_layers: tuple = REGISTER_ATTENTION_LAYERS
+    register_layers: tuple = ()
     cached_layers: tuple = CACHED_LAYERS
     norm_eps: float = 1e-5  # ctx.layernorm's fixed eps (ops.rs:139)
     qk_eps: float = 1e-6
     init_std: float = 0.02
     ls_init: float = 1e-5
+
+    @classmethod
+    def headshot_shared(cls, **overrides) -> "AggregatorConfig":
+        """The reference server's trunk: register-only attention at layers 2, 6, 9, 14, 20
+        (headshot-shared src/model.rs:25-28), 19 global layers."""
+        return cls(**{"register_layers": REGISTER_ATTENTION_LAYERS, **overrides})
 
     @property
     def k_patch(self) -> int:

@@ -57,7 +57,7 @@ def build(verbose: bool = False, ptxas_info: bool = False, force: bool = False) 
         objs.append(obj)
         if not force and not ptxas_info and not _stale(obj, src):
             continue
-        cmd = [cc, *ARCH, *NVCC_FLAGS, "-dc" if False else "-c", str(src), "-o", str(obj)]
+        cmd = [cc, *ARCH, *NVCC_FLAGS, "-c", str(src), "-o", str(obj)]
         if ptxas_info:
             cmd.insert(1, "-Xptxas=-v")
         if verbose:

@@ -96,10 +96,6 @@ extern "C" hs_status hs_attention_fused_noalloc(void* stream, int* status, const
   const uint64_t rows = static_cast<uint64_t>(S) * H * T;
   if (rows * D == 0) return HS_OK;
   if (D != 64) return hs::abi_fail(HS_ERR_UNSUPPORTED, std::string(name) + ": head_dim must be 64");
-  if (rows > HS_NOALLOC_MAX_ROWS)
-    return hs::abi_fail(HS_ERR_INVALID, std::string(name) + ": S*H*T = " + std::to_string(rows) +
-                                            " rows exceeds the fixed scratch of " +
-                                            std::to_string(HS_NOALLOC_MAX_ROWS) + " rows");
   if (static_cast<uint64_t>(S) * H > 65535u)
     return hs::abi_fail(HS_ERR_INVALID, std::string(name) + ": S*H > 65535");
   if (!q || !k || !v || !out) return hs::abi_fail(HS_ERR_INVALID, std::string(name) + ": null tensor pointer");
@@ -110,6 +106,13 @@ extern "C" hs_status hs_attention_fused_noalloc(void* stream, int* status, const
     return hs::abi_fail(HS_ERR_INVALID, std::string(name) + ": QK-norm needs all of q/k weight and bias, or none");
   const bool rope = rope_sin != nullptr;
   if (rope && !rope_cos) return hs::abi_fail(HS_ERR_INVALID, std::string(name) + ": rope_cos missing");
+  // Only the normalised/rotated Q and K rows live in the fixed scratch; with
+  // neither QK-norm nor RoPE the kernel reads q and k directly and any size
+  // the attention kernel takes is accepted.
+  if ((ln || rope) && rows > HS_NOALLOC_MAX_ROWS)
+    return hs::abi_fail(HS_ERR_INVALID, std::string(name) + ": S*H*T = " + std::to_string(rows) +
+                                            " rows exceeds the fixed scratch of " +
+                                            std::to_string(HS_NOALLOC_MAX_ROWS) + " rows");
   const uint32_t tpf = tokens_per_frame ? tokens_per_frame : T;
   if (rope) {
     if (prefix > tpf) return hs::abi_fail(HS_ERR_INVALID, std::string(name) + ": prefix > tokens_per_frame");

@@ -157,13 +157,18 @@ HS_API hs_status hs_attention_block_fused(hs_ctx* ctx, const void* q, const void
  * stream) of the current device, and the normalised Q and K live in a fixed
  * array inside the library — 2 x HS_NOALLOC_MAX_ROWS rows of 128 bytes
  * (64 MiB), held by every GPU that loads the library until the process exits.
- * S*H*T above HS_NOALLOC_MAX_ROWS returns HS_ERR_INVALID.
+ * With a QK-norm or RoPE prologue, S*H*T above HS_NOALLOC_MAX_ROWS returns
+ * HS_ERR_INVALID; without either, q and k are read in place and the array
+ * is not used for rows, so there is no row limit.
  * The first call on a device looks up that array's device address (no
  * allocation by this library); make that first call before any stream
  * capture.  All calls on a device share the array, so calls whose work
  * overlaps on the GPU race; order them on one stream.  `status` (device
- * int, may be NULL) is zeroed by each call and receives a nonzero site
- * code if an in-kernel wait timed out. */
+ * int) is zeroed by each call and receives a nonzero site code if an
+ * in-kernel wait timed out.  With status == NULL the site code goes to a
+ * word inside the library that nothing reads: timeouts are then not
+ * reported and the call's output may be incomplete without notice, so pass
+ * a status word wherever a timeout must be seen. */
 #define HS_NOALLOC_MAX_ROWS 262144u
 HS_API hs_status hs_attention_fused_noalloc(void* stream, int* status, const void* q, const void* k, const void* v,
                                             void* out, uint32_t S, uint32_t H, uint32_t T, uint32_t D,

@@ -14,11 +14,22 @@ import numpy as np
 sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
 
 
+def device_inputs(dev, T: int, H: int, dtype: str, seed: int):
+    """q, k, v (1, H, T, 64) drawn on the device (torch generator, N(0,1) f32 rounded to the
+    storage type): the same bytes on every GPU of this type, and fast at config 4's size."""
+    import torch
+
+    tdt = {"bf16": torch.bfloat16, "f16": torch.float16}[dtype]
+    g = torch.Generator(device=dev).manual_seed(seed)
+    return tuple(torch.randn((1, H, T, 64), device=dev, generator=g).to(tdt) for _ in range(3))
+
+
 def run(rank: int, world: int, port: int, outdir: str, T: int, H: int, dtype: str, seed: int, fused: bool,
-        unit: int = 0) -> None:
+        unit: int = 0, gen: str = "np") -> None:
     """unit = 0: head-major (1, H, T_r, 64) shards of hs_shard's token rule (attention_fused);
     unit > 0: the (T_r, H*64) projection layout in shards of whole `unit`-token frames
-    (attention_block)."""
+    (attention_block).  gen = "np": inputs from numpy's generator (small cases); "torch":
+    from device_inputs."""
     import torch
     import torch.distributed as dist
 
@@ -36,9 +47,13 @@ def run(rank: int, world: int, port: int, outdir: str, T: int, H: int, dtype: st
         ctx = GpuContext(rank)
         sess = RingSession(ctx, rank, world)
         tdt = {"bf16": torch.bfloat16, "f16": torch.float16}[dtype]
-        rng = np.random.default_rng(seed)
-        q, k, v = (oracle.round_to(dtype, rng.standard_normal((1, H, T, 64), np.float32)) for _ in range(3))
+        if gen == "torch":
+            q, k, v = device_inputs(dev, T, H, dtype, seed)
+        else:
+            rng = np.random.default_rng(seed)
+            q, k, v = (oracle.round_to(dtype, rng.standard_normal((1, H, T, 64), np.float32)) for _ in range(3))
         if unit:
+            assert gen == "np"
             t0, t1 = sess.unit_shard(T, unit)
 
             def loc(a):  # (1, H, T, 64) -> this rank's (T_r, H*64) rows
@@ -48,7 +63,10 @@ def run(rank: int, world: int, port: int, outdir: str, T: int, H: int, dtype: st
             out = torch.empty((t1 - t0, H * 64), dtype=tdt, device=dev)
         else:
             t0, t1 = sess.shard(T)
-            loc = lambda a: torch.from_numpy(np.ascontiguousarray(a[:, :, t0:t1])).to(dev).to(tdt)  # noqa: E731
+            if gen == "torch":
+                loc = lambda a: a[:, :, t0:t1].contiguous()  # noqa: E731
+            else:
+                loc = lambda a: torch.from_numpy(np.ascontiguousarray(a[:, :, t0:t1])).to(dev).to(tdt)  # noqa: E731
             out = torch.empty((1, H, t1 - t0, 64), dtype=tdt, device=dev)
         norm = rope = None
         if fused:
@@ -75,4 +93,4 @@ def run(rank: int, world: int, port: int, outdir: str, T: int, H: int, dtype: st
 if __name__ == "__main__":
     a = sys.argv[1:]
     run(int(a[0]), int(a[1]), int(a[2]), a[3], int(a[4]), int(a[5]), a[6], int(a[7]), a[8] == "1",
-        int(a[9]) if len(a) > 9 else 0)
+        int(a[9]) if len(a) > 9 else 0, a[10] if len(a) > 10 else "np")

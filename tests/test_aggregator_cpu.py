@@ -51,9 +51,13 @@ def test_flops_match_the_config5_figures():
     t = 37 * 37 + 5
     glob = 4 * 16 * (100 * t) ** 2 * 64
     assert abs(glob - 7.73e13) / 7.73e13 < 0.01
-    n_global = cfg.trunk_pairs - len(cfg.register_layers)
-    assert f["attention"] > n_global * glob
+    assert cfg.register_layers == () and cfg.trunk_pairs == 24  # config 5: 24 global layers
+    assert f["attention"] > 24 * glob
     assert f["total"] == f["gemm"] + f["attention"]
+    shared = AggregatorConfig.headshot_shared()
+    assert shared.register_layers == (2, 6, 9, 14, 20)
+    fs = Aggregator.flops(type("A", (), {"cfg": shared})(), 100, 518, 518)
+    assert 19 * glob < fs["attention"] < 20 * glob
 
 
 def _free_port() -> int:

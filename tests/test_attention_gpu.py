@@ -353,3 +353,66 @@ def test_repeated_calls_are_bit_identical(gpu_ctx, dtype):
         again = gpu_ctx.attention_fused(qd, kd, vd, qk_norm=norm, rope=rope)
         gpu_ctx.sync()
         assert torch.equal(first, again), f"call {i + 1} differs from the first"
+
+
+# ---- BASELINE configurations at their own sizes (sampled query rows) --------
+#
+# The bench's workloads, generated exactly as bench.py generates them on rank 0
+# (torch generator on the device, seed * 1000, N(0,1) f32 rounded to the
+# storage type), run through hs_attention_fused at full size.  Rows are
+# independent, so a fixed sample of query rows (spread over sequences, the
+# first and last 256-row items, the short tail item, frame boundaries and the
+# unrotated special tokens) is checked against the oracle over every key of
+# its sequence (oracle.attention_rows, attention.wesl:36-82).
+
+def _config_inputs(s, h, t, dtype, seed):
+    dev = torch.device("cuda", torch.cuda.current_device())
+    g = torch.Generator(device=dev).manual_seed(seed * 1000)
+    return tuple(torch.randn((s, h, t, 64), device=dev, dtype=torch.float32, generator=g).to(TORCH[dtype])
+                 for _ in range(3))
+
+
+def _sample_rows(s, h, t, tpf, prefix, n=512, seed=0):
+    """Flattened (s*h + head) * t + token indices: fixed edge positions plus random fill."""
+    rng = np.random.default_rng(seed)
+    seqs = s * h
+    tail0 = (t // 256) * 256 if t % 256 else t - 256  # first row of the last (short) 256-row item
+    edge_tokens = sorted({0, 1, prefix - 1, prefix, 127, 128, 255, 256, tail0, tail0 + 1, t - 2, t - 1,
+                          tpf - 1, min(tpf, t - 1), min(tpf + prefix, t - 1), t // 2} & set(range(t)))
+    edge_seqs = sorted({0, 1, h - 1, seqs // 2, seqs - 1})
+    rows = {sq * t + tok for sq in edge_seqs for tok in edge_tokens}
+    rows |= {int(sq) * t + int(tok) for sq, tok in zip(rng.integers(0, seqs, 64), rng.integers(tail0, t, 64))}
+    while len(rows) < n:
+        rows.add(int(rng.integers(0, seqs)) * t + int(rng.integers(0, t)))
+    return np.array(sorted(rows)[:n], np.int64)
+
+
+@pytest.mark.parametrize("name,s,h,t,dtype,seed,gain", [
+    ("config2_global43k", 1, 16, 32 * 1374, "bf16", 1, 1.0),
+    ("config3_frames200", 200, 16, 1374, "f16", 2, 1.0),
+    ("config4_global274k", 1, 16, 200 * 1374, "bf16", 3, 1.0),
+    # QK-norm gain 1.2 lifts the f16 score bound to ~16.6 > 14: the running-max softmax at config 3's size
+    ("config3_running_max", 200, 16, 1374, "f16", 2, 1.2),
+])
+def test_baseline_config_full_size(gpu_ctx, name, s, h, t, dtype, seed, gain):
+    tpf, prefix, eps = 1374, 5, 1e-6
+    q, k, v = _config_inputs(s, h, t, dtype, seed)
+    sin, cos = oracle.rope_tables(37, 37)
+    w = np.full(64, gain, np.float32)
+    b = np.zeros(64, np.float32)
+    c = lambda a: torch.from_numpy(a).cuda()  # noqa: E731
+    out = gpu_ctx.attention_fused(q, k, v, qk_norm=QkNorm(c(w), c(b), c(w), c(b), eps),
+                                  rope=Rope(c(sin), c(cos), prefix, tpf))
+    gpu_ctx.sync()
+    rows = _sample_rows(s, h, t, tpf, prefix)
+    ours = host(out.reshape(-1, 64)[torch.from_numpy(rows).cuda()])
+    del out
+    qh, kh, vh = (host(x) for x in (q, k, v))
+    del q, k, v
+    # q' and k' rounded to the storage type, as the reference's separate kernels store them
+    qn = rounded(oracle.qk_prep(qh, w, b, eps, sin, cos, prefix, tpf), dtype)
+    del qh
+    kn = rounded(oracle.qk_prep(kh, w, b, eps, sin, cos, prefix, tpf), dtype)
+    del kh
+    ref = oracle.attention_rows(qn, kn, vh, rows)
+    gate(ours, ref)
