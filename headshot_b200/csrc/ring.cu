@@ -97,6 +97,8 @@ void shard(uint32_t n, int world, int rank, uint32_t* start, uint32_t* len) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+constexpr uint32_t kDefaultReservedSms = 4;
+
 }  // namespace
 
 struct hs_ring {
@@ -120,6 +122,11 @@ struct hs_ring {
   uint8_t* state = nullptr;
   size_t state_rows = 0;
   bool aborted = false;
+  // SMs the attention kernel leaves free during ring steps.  The kernel is
+  // persistent and takes a whole SM per CTA (shared memory and registers), so
+  // without free SMs NCCL's send/recv kernel for the next block would wait for
+  // the attention launch to end and every transfer would add to the step.
+  uint32_t reserved_sms = kDefaultReservedSms;
 };
 
 extern "C" {
@@ -186,6 +193,14 @@ hs_status hs_ring_create(hs_ctx* ctx, int rank, int world, const void* id, hs_ri
     return hs::abi_cuda_fail(e, "hs_ring_create");
   }
   *out = ring;
+  return HS_OK;
+}
+
+hs_status hs_ring_set_reserved_sms(hs_ring* ring, uint32_t sms) {
+  if (!ring) return hs::abi_fail(HS_ERR_INVALID, "hs_ring_set_reserved_sms: null ring");
+  if (sms + 1 > static_cast<uint32_t>(ring->ctx->sm_count))
+    return hs::abi_fail(HS_ERR_INVALID, "hs_ring_set_reserved_sms: must leave at least one SM for attention");
+  ring->reserved_sms = sms;
   return HS_OK;
 }
 
@@ -375,6 +390,7 @@ hs_status ring_attention(hs_ring* ring, const void* q, const void* k, const void
       shard_of(nsrc, &n_t0, &n_len);
       if (s == 0) cudaStreamWaitEvent(cs, ring->ev_block0, 0);
       if (s >= 1) cudaStreamWaitEvent(cs, ring->ev_compute[(s - 1) % 2], 0);  // nxt was read by step s-1
+      hs::ProfScope prof(ctx, cs, "ring_transfer");
       ncclResult_t nr = n.GroupStart();
       if (nr == ncclSuccess) nr = n.Send(cur, 2ull * H * src_len * row_bytes, ncclUint8, send_to, ring->comm, cs);
       if (nr == ncclSuccess) nr = n.Recv(nxt, 2ull * H * n_len * row_bytes, ncclUint8, recv_from, ring->comm, cs);
@@ -399,7 +415,8 @@ hs_status ring_attention(hs_ring* ring, const void* q, const void* k, const void
       io.out = out;
       io.lo = given(tr);
       io.out_code = code;
-      e = hs::launch_attention_sm100(st, code, io, 1, H, tr, src_len, scale, state, 0, ctx->d_status, ctx->d_sched,
+      const uint32_t ctas = static_cast<uint32_t>(ctx->sm_count) - ring->reserved_sms;
+      e = hs::launch_attention_sm100(st, code, io, 1, H, tr, src_len, scale, state, ctas, ctx->d_status, ctx->d_sched,
                                      bounded ? ring->norm2 : nullptr, true, hs::ctx_timeout_ns(ctx), &err);
     }
     if (e != cudaSuccess)

@@ -37,6 +37,7 @@ RING_SIGNATURES = {
     "hs_ring_attention_block_fused": (_i, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _i, _f32, _vp, _vp, _vp, _vp,
                                            _f32, _vp, _vp, _u32, _u32, _u32, _u32]),
     "hs_ring_sync": (_i, [_vp, _u32]),
+    "hs_ring_set_reserved_sms": (_i, [_vp, _u32]),
 }
 
 
@@ -184,6 +185,10 @@ class RingSession:
             self._h, _ptr(q), _ptr(k), _ptr(v), _ptr(out), heads, T_total, 64, _code(q),
             0.0 if scale is None else float(scale), *pro, shard_unit))
         return out
+
+    def set_reserved_sms(self, sms: int) -> None:
+        """SMs the ring's attention launches leave free for the transfer of the next block."""
+        check(self._L.hs_ring_set_reserved_sms(self._h, int(sms)))
 
     def sync(self, timeout_ms: int = 120_000) -> None:
         check(self._L.hs_ring_sync(self._h, int(timeout_ms)))
