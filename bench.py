@@ -319,6 +319,8 @@ def run_ours(args, wl: dict, rank: int, world: int, local: int) -> dict | None:
             from headshot_b200.session import RingSession
 
             session = RingSession(ctx, rank, world)
+            if args.ring_reserved_sms is not None:
+                session.set_reserved_sms(args.ring_reserved_sms)
 
     g = torch.Generator(device=dev).manual_seed(wl["seed"] * 1000 + rank)
     q, k, v = (torch.randn(shape, device=dev, dtype=torch.float32, generator=g).to(tdt) for _ in range(3))
@@ -362,7 +364,10 @@ def run_ours(args, wl: dict, rank: int, world: int, local: int) -> dict | None:
     ctx.sync()
     ms_local = e0.elapsed_time(e1)
     attn_ms, attn_n = ctx.prof_read("attention")
+    xfer_ms, xfer_n = ctx.prof_read("ring_transfer")
     all_ms, all_n = ctx.prof_read("*")
+    all_ms -= xfer_ms  # transfers run on the ring's own stream, beside the kernels
+    all_n -= xfer_n
     ms = max_over_ranks(ms_local, world)
     ms_per_step = ms / args.steps
     value = flops_total / (ms_per_step / 1e3) / 1e12
@@ -479,6 +484,17 @@ def run_ours(args, wl: dict, rank: int, world: int, local: int) -> dict | None:
                 # device time of this rank's attention launches over the timed region's device time
                 "kernel_share_of_step": round(attn_ms / max(ms_local, 1e-9), 4),
                 "other_launches_ms_per_step": round((all_ms - attn_ms) / args.steps, 3)}
+    if session is not None:
+        # Ring overlap, from events on both streams of this rank: the block transfers
+        # (NCCL send/recv on the ring's stream) and the attention launches.  What the
+        # step spends outside attention launches is what the transfers (and the Q'/K'
+        # prep) did not hide.
+        roofline["ring"] = {
+            "reserved_sms": args.ring_reserved_sms if args.ring_reserved_sms is not None else "library default",
+            "transfers_per_step": round(xfer_n / args.steps, 2),
+            "transfer_ms_per_step": round(xfer_ms / args.steps, 3),
+            "attention_ms_per_step": round(attn_ms / args.steps, 3),
+            "outside_attention_frac": round(1.0 - attn_ms / max(ms_local, 1e-9), 4)}
 
     result = None
     if rank == 0:
@@ -1355,6 +1371,8 @@ def main():
     ap.add_argument("--cpu-threads", type=int, default=0)
     ap.add_argument("--ref-step-seconds", type=float, default=4.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ring-reserved-sms", type=int, default=None,
+                    help="SMs the ring's attention launches leave to the block transfers (default: the library's)")
     args = ap.parse_args()
     if args.warmup < 3:
         log("warmup raised to 3 (timing rule)")

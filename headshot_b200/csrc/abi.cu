@@ -328,8 +328,7 @@ void* hs_ctx_stream(hs_ctx* ctx) { return ctx ? static_cast<void*>(ctx_stream(ct
 
 hs_status hs_ctx_set_wait_timeout_ms(hs_ctx* ctx, uint32_t ms) {
   if (!ctx) return fail(HS_ERR_INVALID, "hs_ctx_set_wait_timeout_ms: null context");
-  if (ms == 0) return fail(HS_ERR_INVALID, "hs_ctx_set_wait_timeout_ms: timeout must be > 0");
-  ctx->wait_timeout_ms = ms;
+  ctx->wait_timeout_ms = ms;  // 0: kernels do not wait (see the header)
   return HS_OK;
 }
 

@@ -516,16 +516,15 @@ __device__ void producer_role(const Args& a, const CUtensorMap* tm_q, const CUte
     }
   }
   // Let every load this thread issued land before the CTA can exit (on the
-  // normal path they have all been consumed already).
-  int no_abort = 0;
+  // normal path they have all been consumed already); fixed teardown bound.
   const uint32_t first = g > kStages ? g - kStages : 0;
   for (uint32_t t = first; t < g; ++t)
-    mbar_wait(&ctl->kv_full[t % kStages], (t / kStages) & 1, &no_abort, a.status, kSiteKvFull, a.timeout_ns);
+    mbar_wait_teardown(&ctl->kv_full[t % kStages], (t / kStages) & 1, a.status, kSiteKvFull);
 #pragma unroll
   for (int wg = 0; wg < 2; ++wg) {
     const uint32_t qi = q_issued[wg];
     for (uint32_t t = qi > kQBufs ? qi - kQBufs : 0; t < qi; ++t)
-      mbar_wait(&ctl->q_full[wg][t % kQBufs], (t / kQBufs) & 1, &no_abort, a.status, kSiteQFull, a.timeout_ns);
+      mbar_wait_teardown(&ctl->q_full[wg][t % kQBufs], (t / kQBufs) & 1, a.status, kSiteQFull);
   }
 }
 
@@ -635,10 +634,12 @@ __device__ void mma_role(const Args& a, int wg, uint8_t* sQ, uint8_t* sK, uint8_
     p_base1 += n >> 1;
     ++q_used;
   }
-  // Drain: every MMA this warp issued has completed before TMEM is freed.
+  // Drain: every MMA this warp issued has completed before TMEM is freed
+  // (fixed teardown bound, whatever the caller's timeout).
   umma_commit_elect(&ctl->drain[wg]);
-  int no_abort = 0;
-  warp_wait(&ctl->drain[wg], 0, &no_abort, a.status, kSiteODone, a.timeout_ns);
+  const bool drained = mbar_wait_teardown(&ctl->drain[wg], 0, a.status, kSiteODone);
+  __syncwarp();
+  (void)drained;
 }
 
 template <typename E>

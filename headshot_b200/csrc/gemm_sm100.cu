@@ -64,7 +64,6 @@ struct Ctrl {
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
-  int no_abort;
 };
 
 constexpr int kStageOutBytes = 32 * 32 * 2;  // one warp's 32x32 16-bit output block
@@ -170,7 +169,7 @@ __device__ void producer_role(const Args& a, const CUtensorMap* tm_a, const CUte
   }
   const uint32_t first = g > kStages ? g - kStages : 0;
   for (uint32_t t = first; t < g; ++t)
-    mbar_wait(&ctl->full[t % kStages], (t / kStages) & 1, &ctl->no_abort, a.status, kSiteFull, a.timeout_ns);
+    mbar_wait_teardown(&ctl->full[t % kStages], (t / kStages) & 1, a.status, kSiteFull);
 }
 
 template <bool kBf16>
@@ -207,7 +206,8 @@ __device__ void mma_role(const Args& a, uint8_t* sA, uint8_t* sB, Ctrl* ctl, uin
     if (ok) umma_commit_elect(&ctl->acc_full[ab]);
   }
   umma_commit_elect(&ctl->drain);
-  warp_wait(&ctl->drain, 0, &ctl->no_abort, a.status, kSiteDrain, a.timeout_ns);
+  mbar_wait_teardown(&ctl->drain, 0, a.status, kSiteDrain);
+  __syncwarp();
 }
 
 template <typename E>
@@ -223,7 +223,8 @@ __device__ void epilogue_role(const Args& a, const CUtensorMap* tm_out, uint8_t*
   uint32_t i = 0;
   for (uint32_t tile = blockIdx.x; tile < a.n_tiles_total; tile += gridDim.x, ++i) {
     const uint32_t ab = i & 1;
-    if (!warp_wait(&ctl->acc_full[ab], (i >> 1) & 1, abort_flag, a.status, kSiteAccFull, a.timeout_ns)) return;
+    // On a timeout, leave the loop but still wait for this warp's stores below.
+    if (!warp_wait(&ctl->acc_full[ab], (i >> 1) & 1, abort_flag, a.status, kSiteAccFull, a.timeout_ns)) break;
     tc_fence_after();
     const uint64_t row = static_cast<uint64_t>(tile / a.n_tiles) * kBM + row_in_tile;
     const uint32_t n0 = (tile % a.n_tiles) * kBN;
@@ -322,7 +323,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(&ctl->drain, 1);
     ctl->abort_flag = 0;
-    ctl->no_abort = 0;
     fence_mbar_init();
   }
   if (warp == kProducerWarp && lane == 0) {

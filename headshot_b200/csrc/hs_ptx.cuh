@@ -59,6 +59,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking test of the phase with parity `parity` (never suspends).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait for the phase with parity `parity` to complete.
 // Returns false on timeout or when the CTA abort flag is up.  The first
 // kFastSpins polls touch nothing else.  An isolated mbarrier round trip is
@@ -68,8 +81,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // there (1, 4, 16, 64 polls: 835, 806, 804, 787 TFLOP/s).
 constexpr uint32_t kFastSpins = 1;
 
+//
+// timeout_ns == 0 means "do not wait": a phase that is not complete when
+// first tested (test_wait, which never suspends the thread) counts as timed
+// out.  hs_ctx_set_wait_timeout_ms(ctx, 0) selects it, so that a test can
+// drive every kernel's timeout path deterministically without a fault.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           int* status, int site, uint64_t timeout_ns) {
+  if (timeout_ns == 0) {
+    if (mbar_test_wait(bar, parity)) return true;
+    *abort_flag = 1;
+    atomicCAS(status, 0, site);
+    return false;
+  }
 #pragma unroll 1
   for (uint32_t it = 0; it < kFastSpins; ++it)
     if (mbar_try_wait(bar, parity)) return true;
@@ -85,6 +109,18 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
       }
     }
   }
+}
+
+// Teardown waits (a CTA's own TMA loads and MMAs in flight, before it frees
+// TMEM and exits) have a fixed bound of their own, independent of the
+// caller's timeout: however short that is, a CTA never leaves with a copy
+// into its shared memory or a tensor-core write to its TMEM outstanding.
+// They ignore the abort flag for the same reason.
+constexpr uint64_t kTeardownTimeoutNs = 4000ull * 1000000ull;
+
+__device__ __forceinline__ bool mbar_wait_teardown(uint64_t* bar, uint32_t parity, int* status, int site) {
+  int no_abort = 0;
+  return mbar_wait(bar, parity, &no_abort, status, site, kTeardownTimeoutNs);
 }
 
 // Warpgroup register reallocation (all 128 threads of the warpgroup execute it).

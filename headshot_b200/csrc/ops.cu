@@ -386,11 +386,10 @@ __global__ void __launch_bounds__(kTpBlockThreads, kTpBlocksPerSm)
         issue(u, st);
       }
       // Let the last loads land before the block can exit (on the normal path
-      // the compute warps have consumed them already).
-      int no_abort = 0;
+      // the compute warps have consumed them already); fixed teardown bound.
       for (uint64_t k = n > kTpStages ? n - kTpStages : 0; k < n; ++k)
-        mbar_wait(&full[k % kTpStages], static_cast<uint32_t>(k / kTpStages) & 1u, &no_abort, a.status,
-                  kSitePrepFull, a.timeout_ns);
+        mbar_wait_teardown(&full[k % kTpStages], static_cast<uint32_t>(k / kTpStages) & 1u, a.status,
+                           kSitePrepFull);
     }
     return;
   }

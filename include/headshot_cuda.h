@@ -71,7 +71,13 @@ HS_API hs_status hs_ctx_set_stream(hs_ctx* ctx, void* stream);
 HS_API hs_status hs_ctx_use_own_stream(hs_ctx* ctx);
 HS_API void* hs_ctx_stream(hs_ctx* ctx);
 
-/* Upper bound for every in-kernel wait, in milliseconds (default 2000). */
+/* Upper bound for every in-kernel wait, in milliseconds (default 2000).
+ * A wait that gives up records a site code; the kernel's CTAs then stop,
+ * let their own copies and tensor-core work in flight finish (a fixed bound
+ * of 4 s of their own) and exit, and hs_sync returns HS_ERR_TIMEOUT with the
+ * context still usable.  ms = 0 means "do not wait": a wait whose condition
+ * does not already hold gives up at once, which drives every call into that
+ * path deterministically (for testing the timeout handling). */
 HS_API hs_status hs_ctx_set_wait_timeout_ms(hs_ctx* ctx, uint32_t ms);
 
 /* Cooperative cancellation (src/engine/mod.rs:92-95, :286-304): multi-step
