@@ -9,8 +9,11 @@
 // of the fused op has already been applied to q and k by qk_prep (ops.cu).
 //
 // The kernel is persistent: one CTA per SM takes work items from a global
-// counter (the producer thread fetches the next index one item ahead and
-// hands it to the other warps through a small ring in shared memory).  An
+// counter (the producer thread fetches the next index one item ahead, decodes
+// it into (sequence, first row) and hands that to the other warps through a
+// small ring in shared memory; the MMA warps take the next item as soon as
+// they have issued an item's last score product, the softmax warps while the
+// item's last PV product runs, so the hand-off stays off the item boundary).  An
 // item is 256 query rows of one (s, h) sequence, split into two 128-row
 // tiles, one per softmax warpgroup, against every 96-key K/V tile of that
 // sequence.  Items go out in sequence-major order, so the CTAs working at
@@ -119,7 +122,8 @@ struct Ctrl {
   uint64_t drain[2];              // every MMA of that warpgroup's MMA warp completed
   uint64_t item_full[kItemSlots];   // the producer wrote an item index into the slot
   uint64_t item_empty[kItemSlots];  // every reader took it
-  uint32_t item_slot[kItemSlots];   // item index; >= n_items means no more work
+  uint32_t item_seq[kItemSlots];    // decoded item: sequence s*heads+h (kNoItem: no more work)
+  uint32_t item_row0[kItemSlots];   // first query row of the item
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -164,6 +168,8 @@ __device__ __forceinline__ Item decode_item(const Args& a, uint32_t item) {
 
 __device__ __forceinline__ float u2f(uint32_t u) { return __uint_as_float(u); }
 
+constexpr uint32_t kNoItem = 0xffffffffu;
+
 // Position in the K/V stage ring: stage index and the parity of its use count.
 struct RingPos {
   uint32_t stage = 0;
@@ -187,12 +193,13 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
 // Next item index for a reader warp (all lanes): waits for slot k % kItemSlots,
 // reads it, and releases the slot with one arrival per warp.  Returns false
 // on timeout/abort.
-__device__ __forceinline__ bool next_item(const Args& a, Ctrl* ctl, uint32_t k, uint32_t* item) {
+__device__ __forceinline__ bool next_item(const Args& a, Ctrl* ctl, uint32_t k, Item* item) {
   const uint32_t slot = k % kItemSlots;
   if (!warp_wait(&ctl->item_full[slot], (k / kItemSlots) & 1, &ctl->abort_flag, a.status, kSiteItemFull,
                  a.timeout_ns))
     return false;
-  *item = *reinterpret_cast<volatile uint32_t*>(&ctl->item_slot[slot]);
+  item->seq = *reinterpret_cast<volatile uint32_t*>(&ctl->item_seq[slot]);
+  item->row0 = *reinterpret_cast<volatile uint32_t*>(&ctl->item_row0[slot]);
   __syncwarp();
   if ((threadIdx.x & 31) == 0) mbar_arrive(&ctl->item_empty[slot]);
   return true;
@@ -266,11 +273,17 @@ __device__ void softmax_role(const Args& a, Ctrl* ctl, uint32_t tmem, int warp, 
   uint32_t base_bits = 0;
   auto s_parity = [&](uint32_t t) { return ((base_bits >> (t & 1)) + (t >> 1)) & 1; };
 
+  Item nxt{};
+  bool have_nxt = false;
   for (uint32_t k = 0;; ++k) {
-    uint32_t item;
-    if (!next_item(a, ctl, k, &item)) return;
-    if (item >= a.n_items) break;
-    const Item it = decode_item(a, item);
+    Item it;
+    if (have_nxt) {
+      it = nxt;
+      have_nxt = false;
+    } else if (!next_item(a, ctl, k, &it)) {
+      return;
+    }
+    if (it.seq == kNoItem) break;
     const uint32_t tile0 = it.row0 + wg * kBM;
     if (tile0 >= a.t_q) continue;  // this warpgroup has no rows in the item
     const uint32_t token = tile0 + row;
@@ -394,6 +407,9 @@ __device__ void softmax_role(const Args& a, Ctrl* ctl, uint32_t tmem, int warp, 
       if (lane == 0) mbar_arrive(&ctl->p_full[wg][b]);
     }
 
+    // The next item's hand-off while PV(n-1) runs.
+    if (!next_item(a, ctl, k + 1, &nxt)) return;
+    have_nxt = true;
     // PV(n-1) and every MMA before it have completed: the item's pv_last.
     if (!warp_wait(&ctl->pv_last[wg], (base_bits >> 2) & 1, abort_flag, a.status, kSiteODone, a.timeout_ns))
       return;
@@ -480,10 +496,11 @@ __device__ void producer_role(const Args& a, const CUtensorMap* tm_q, const CUte
     if (k >= kItemSlots && !mbar_wait(&ctl->item_empty[slot], ((k / kItemSlots) - 1) & 1, abort_flag, a.status,
                                       kSiteItemEmpty, a.timeout_ns))
       break;
-    ctl->item_slot[slot] = item;
-    mbar_arrive(&ctl->item_full[slot]);  // release: the index is visible to the readers' acquire
-    if (item >= a.n_items) break;
-    const Item it = decode_item(a, item);
+    const Item it = item < a.n_items ? decode_item(a, item) : Item{kNoItem, 0};
+    ctl->item_seq[slot] = it.seq;
+    ctl->item_row0[slot] = it.row0;
+    mbar_arrive(&ctl->item_full[slot]);  // release: the item is visible to the readers' acquire
+    if (it.seq == kNoItem) break;
     item = gridDim.x + atomicAdd(a.sched, 1u);  // used one item later: the latency hides behind the loads
 #pragma unroll
     for (int wg = 0; wg < 2; ++wg) {
@@ -571,11 +588,26 @@ __device__ void mma_role(const Args& a, int wg, uint8_t* sQ, uint8_t* sK, uint8_
     return warp_wait(&ctl->kv_full[r.stage], r.phase, abort_flag, a.status, kSiteKvFull, a.timeout_ns);
   };
 
+  // The next item is fetched as soon as the current one's last S product is
+  // issued, so the hand-off is off the path from PV(n-1) to the next S(0).
+  Item nxt{};
+  bool have_nxt = false;
+  auto fetch_next = [&](uint32_t k_next) {
+    if (!have_nxt) {
+      if (!next_item(a, ctl, k_next, &nxt)) return false;
+      have_nxt = true;
+    }
+    return true;
+  };
   for (uint32_t k = 0; ok; ++k) {
-    uint32_t item;
-    if (!next_item(a, ctl, k, &item)) break;
-    if (item >= a.n_items) break;
-    const Item it = decode_item(a, item);
+    Item it;
+    if (have_nxt) {
+      it = nxt;
+      have_nxt = false;
+    } else if (!next_item(a, ctl, k, &it)) {
+      break;
+    }
+    if (it.seq == kNoItem) break;
     if (it.row0 + wg * kBM >= a.t_q) {
       // No rows for this warpgroup: release each stage once it has landed
       // (waiting keeps this warp's view of the ring phases exact).
@@ -603,7 +635,10 @@ __device__ void mma_role(const Args& a, int wg, uint8_t* sQ, uint8_t* sK, uint8_
       issue_s(q_desc, s_pos.stage, static_cast<int>(t));
       s_pos.next();
       umma_commit_elect(&ctl->s_full[wg][t]);
-      if (t == n - 1) umma_commit_elect(&ctl->q_empty[wg][qb]);
+      if (t == n - 1) {
+        umma_commit_elect(&ctl->q_empty[wg][qb]);
+        if (!fetch_next(k + 1)) ok = false;
+      }
     }
     for (uint32_t j = 0; ok && j < n; ++j) {
       const int b = static_cast<int>(j & 1);
@@ -624,7 +659,13 @@ __device__ void mma_role(const Args& a, int wg, uint8_t* sQ, uint8_t* sK, uint8_
         issue_s(q_desc, s_pos.stage, b);  // after PV(j) in this warp's order: P(j) is read first
         s_pos.next();
         umma_commit_elect(&ctl->s_full[wg][b]);
-        if (j + 2 == n - 1) umma_commit_elect(&ctl->q_empty[wg][qb]);
+        if (j + 2 == n - 1) {
+          umma_commit_elect(&ctl->q_empty[wg][qb]);
+          if (!fetch_next(k + 1)) {
+            ok = false;
+            break;
+          }
+        }
       } else {
         umma_commit_elect(j + 1 == n ? &ctl->pv_last[wg] : &ctl->pv_prev[wg]);
       }

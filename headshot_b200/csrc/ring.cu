@@ -97,7 +97,9 @@ void shard(uint32_t n, int world, int rank, uint32_t* start, uint32_t* len) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-constexpr uint32_t kDefaultReservedSms = 4;
+// Default SMs left to the block transfers: none at 2 ranks (one transfer
+// per call, measured fastest with every SM on attention), 4 beyond.
+uint32_t default_reserved_sms(int world) { return world > 2 ? 4u : 0u; }
 
 }  // namespace
 
@@ -124,9 +126,11 @@ struct hs_ring {
   bool aborted = false;
   // SMs the attention kernel leaves free during ring steps.  The kernel is
   // persistent and takes a whole SM per CTA (shared memory and registers), so
-  // without free SMs NCCL's send/recv kernel for the next block would wait for
-  // the attention launch to end and every transfer would add to the step.
-  uint32_t reserved_sms = kDefaultReservedSms;
+  // without free SMs NCCL's send/recv kernel for the next block waits for the
+  // attention launch to end and every transfer adds to the step.  Freeing SMs
+  // costs attention throughput in proportion; it pays when the transfers are
+  // large next to the launches (many ranks, short shards).
+  uint32_t reserved_sms = 0;
 };
 
 extern "C" {
@@ -175,6 +179,7 @@ hs_status hs_ring_create(hs_ctx* ctx, int rank, int world, const void* id, hs_ri
   ring->ctx = ctx;
   ring->rank = rank;
   ring->world = world;
+  ring->reserved_sms = default_reserved_sms(world);
   ncclUniqueId uid;
   memcpy(&uid, id, sizeof uid);
   ncclResult_t r = n.CommInitRank(&ring->comm, world, uid, rank);
