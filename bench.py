@@ -104,8 +104,10 @@ WORKLOADS = {
 # the attention kernel's sources at capture time: a figure whose hash no longer
 # matches the sources is not reported (traffic null, with the reason).
 MEASURED_TRAFFIC = {
-    "global": {"bytes": 12.26e9 + 574.90e6, "sources_sha256": None},
-    "global43k": {"bytes": 270.41e6 + 75.09e6, "sources_sha256": None},
+    "global": {"bytes": 15683490816 + 575663360,
+               "sources_sha256": "217bb98b58d6f66f418e5ca60fc1b483f14fa0f96e0d3ace2a7341f5a72a3368"},
+    "global43k": {"bytes": 270921984 + 74107392,
+                  "sources_sha256": "217bb98b58d6f66f418e5ca60fc1b483f14fa0f96e0d3ace2a7341f5a72a3368"},
 }
 TRAFFIC_SOURCES = ("headshot_b200/csrc/attention_sm100.cu", "headshot_b200/csrc/hs_ptx.cuh")
 
