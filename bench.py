@@ -488,13 +488,15 @@ def run_ours(args, wl: dict, rank: int, world: int, local: int) -> dict | None:
                 "other_launches_ms_per_step": round((all_ms - attn_ms) / args.steps, 3)}
     if session is not None:
         # Ring overlap, from events on both streams of this rank: the block transfers
-        # (NCCL send/recv on the ring's stream) and the attention launches.  What the
-        # step spends outside attention launches is what the transfers (and the Q'/K'
-        # prep) did not hide.
+        # (NCCL send/recv on the ring's stream) and the attention launches.  A transfer's
+        # span runs from the point its stream reaches it (the previous step's attention
+        # launch has been queued) to its completion, so it includes any wait for SMs.
+        # What the step spends outside attention launches is what the transfers, the
+        # Q'/K' prep and the launches' own tails did not hide.
         roofline["ring"] = {
-            "reserved_sms": args.ring_reserved_sms if args.ring_reserved_sms is not None else "library default",
+            "reserved_sms": args.ring_reserved_sms if args.ring_reserved_sms is not None else "library default (0)",
             "transfers_per_step": round(xfer_n / args.steps, 2),
-            "transfer_ms_per_step": round(xfer_ms / args.steps, 3),
+            "transfer_span_ms_per_step": round(xfer_ms / args.steps, 3),
             "attention_ms_per_step": round(attn_ms / args.steps, 3),
             "outside_attention_frac": round(1.0 - attn_ms / max(ms_local, 1e-9), 4)}
 

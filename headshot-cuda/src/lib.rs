@@ -353,7 +353,7 @@ impl Ring {
         Ok(Ring { raw, ctx: ctx.clone() })
     }
 
-    /// SMs the attention launches leave to the block transfers (default 0 at 2 ranks, 4 beyond).
+    /// SMs the attention launches leave to the block transfers (default 0).
     pub fn set_reserved_sms(&self, sms: u32) -> Result<(), Error> {
         check(unsafe { ffi::hs_ring_set_reserved_sms(self.raw, sms) })
     }

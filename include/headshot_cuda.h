@@ -246,8 +246,8 @@ HS_API hs_status hs_ring_create(hs_ctx* ctx, int rank, int world, const void* id
 HS_API hs_status hs_ring_destroy(hs_ring* ring);
 /* SMs the ring's attention launches leave free, so that the NCCL kernel
  * moving the next [K'|V] block runs alongside the attention kernel instead
- * of between launches; 0 gives attention every SM.  Default: 0 for a ring
- * of 2 ranks, 4 for more.  Must leave at least one SM for attention. */
+ * of between launches; 0 (the default) gives attention every SM.  Must
+ * leave at least one SM for attention. */
 HS_API hs_status hs_ring_set_reserved_sms(hs_ring* ring, uint32_t sms);
 /* Global attention over the ring, arguments as hs_attention_fused with
  * S = 1; RoPE positions use each token's global index. f16/bf16 only. */
