@@ -47,6 +47,7 @@ def lib() -> ctypes.CDLL:
         u32, u64, f32 = ctypes.c_uint32, ctypes.c_uint64, ctypes.c_float
         L.or_rng_uniform.argtypes = [u64, _f32p, u64]
         L.or_rng_normal.argtypes = [u64, _f32p, u64]
+        L.or_rng_f16_exact.argtypes = [u64, _f32p, u64]
         L.or_round_to.argtypes = [ctypes.c_int, _f32p, _f32p, u64]
         L.or_rope_periods.argtypes = [_f32p]
         L.or_rope_tables.argtypes = [_f32p, ctypes.c_int, ctypes.c_int, _f32p, _f32p]
@@ -94,6 +95,14 @@ def rng_normal(seed: int, n: int) -> np.ndarray:
     """Seeded N(0,1): SplitMix64 + Box-Muller."""
     out = np.empty(n, np.float32)
     lib().or_rng_normal(seed, _p(out), n)
+    return out
+
+
+def rng_f16_exact(seed: int, n: int) -> np.ndarray:
+    """tests/f16_ops.rs:7-19: SplitMix64 without the final xorshift, (z>>40)/2^24*2-1 in [-1, 1),
+    rounded to f16 (values every storage type holds exactly)."""
+    out = np.empty(n, np.float32)
+    lib().or_rng_f16_exact(seed, _p(out), n)
     return out
 
 

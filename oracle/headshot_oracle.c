@@ -141,6 +141,20 @@ OR_API void or_round_to(int dtype, const float *x, float *out, uint64_t n) {
     }
 }
 
+/* tests/f16_ops.rs:7-19 (the f16-vs-f32 test's own generator): the SplitMix64
+ * step without its final xorshift, (z >> 40) / 2^24 * 2 - 1 in [-1, 1), then
+ * rounded to f16, so both storage types hold the same values. */
+OR_API void or_rng_f16_exact(uint64_t seed, float *out, uint64_t n) {
+    uint64_t s = seed;
+    for (uint64_t i = 0; i < n; ++i) {
+        s += 0x9E3779B97F4A7C15ull;
+        uint64_t z = s;
+        z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+        z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+        out[i] = or_f16_to_f32(or_f32_to_f16((float)(z >> 40) / (float)(1ull << 24) * 2.0f - 1.0f));
+    }
+}
+
 /* --------------------------------------------------------------- RoPE --- */
 
 /* rope.rs:8-10: periods[i] = 100^(2i/32) in f32. */

@@ -22,6 +22,23 @@ def test_rng_matches_golden(seed):
     np.testing.assert_array_equal(oracle.rng_uniform(seed, 64), GOLDEN[f"rng_{seed}"])
 
 
+def test_rng_f16_exact_generator():
+    """tests/f16_ops.rs:7-19: SplitMix64 without the final xorshift, (z>>40)/2^24*2-1, rounded
+    to f16; restated here independently with Python integers for the first values."""
+    mask = (1 << 64) - 1
+    s, want = 7, []
+    for _ in range(64):
+        s = (s + 0x9E3779B97F4A7C15) & mask
+        z = ((s ^ (s >> 30)) * 0xBF58476D1CE4E5B9) & mask
+        z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & mask
+        want.append(np.float16(np.float32((z >> 40) / float(1 << 24) * 2.0 - 1.0)))
+    got = oracle.rng_f16_exact(7, 64)
+    np.testing.assert_array_equal(got, np.array(want, np.float32))
+    many = oracle.rng_f16_exact(1, 1 << 16)
+    assert many.min() >= -1.0 and many.max() <= 1.0
+    np.testing.assert_array_equal(many, many.astype(np.float16).astype(np.float32))
+
+
 def test_rng_normal_moments():
     x = oracle.rng_normal(1, 200_000)
     assert abs(float(x.mean())) < 0.01 and abs(float(x.std()) - 1.0) < 0.01
