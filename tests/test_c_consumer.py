@@ -135,3 +135,54 @@ def test_rust_binding_matches_header():
         r_ret, r_params = rust[name]
         assert r_ret == ret, f"{name}: returns {r_ret}, header says {ret}"
         assert r_params == params, f"{name}: parameters {r_params}, header says {params}"
+
+
+# ---- the crate's safe layer against its own declarations --------------------
+
+LIB_RS = ROOT / "headshot-cuda" / "src" / "lib.rs"
+PATCH_RS = ROOT / "headshot-cuda" / "patches" / "engine_attention.rs"
+
+
+def _call_args(text: str, start: int) -> list[str]:
+    """Top-level comma-separated arguments of the call whose '(' is at text[start]."""
+    depth, args, cur = 0, [], []
+    for ch in text[start:]:
+        if ch in "([{":
+            depth += 1
+            if depth == 1:
+                continue
+        elif ch in ")]}":
+            depth -= 1
+            if depth == 0:
+                if "".join(cur).strip():
+                    args.append("".join(cur).strip())
+                return args
+        if depth == 1 and ch == ",":
+            args.append("".join(cur).strip())
+            cur = []
+        elif depth >= 1:
+            cur.append(ch)
+    raise AssertionError("unbalanced call")
+
+
+def test_safe_layer_calls_declared_functions_with_their_arity():
+    """The crate is not compiled here (no Rust toolchain): every ffi::hs_* call in src/lib.rs
+    must name a function src/ffi.rs declares and pass as many arguments as it takes."""
+    declared = _rust_decls()
+    text = LIB_RS.read_text()
+    calls = [(m.group(1), m.end() - 1) for m in re.finditer(r"ffi::(hs_\w+)\(", text)]
+    assert len(calls) >= 15
+    for name, paren in calls:
+        assert name in declared, f"lib.rs calls undeclared {name}"
+        n_args = len(_call_args(text, paren))
+        assert n_args == len(declared[name][1]), f"{name}: {n_args} arguments, ffi.rs declares {len(declared[name][1])}"
+
+
+def test_engine_patch_uses_the_safe_layer():
+    """patches/engine_attention.rs uses only items src/lib.rs defines."""
+    lib = LIB_RS.read_text()
+    patch = PATCH_RS.read_text()
+    for item in set(re.findall(r"headshot_cuda::(\w+)", patch)):
+        assert re.search(rf"pub (struct|fn|enum) {item}\b", lib), f"lib.rs has no pub {item}"
+    for method in set(re.findall(r"\.cuda\.(\w+)\(", patch)):
+        assert re.search(rf"pub fn {method}\(", lib), f"Context has no method {method}"
