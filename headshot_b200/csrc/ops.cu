@@ -467,7 +467,9 @@ __global__ void __launch_bounds__(kTpBlockThreads, kTpBlocksPerSm)
     if (ok) {
       const uint8_t* box0 = stages + st * kTpStageBytes;
       const uint32_t nq = min(static_cast<uint32_t>(kTpSeqs), a.sh - q0);
-#pragma unroll 2
+      // Four of the unit's sequences in flight per thread: -3.7 % time at 200 x 16 x 1374
+      // against two (71 registers, still three blocks per SM).
+#pragma unroll 4
       for (uint32_t j = 0; j < nq; ++j) {
         const uint2 rl = *reinterpret_cast<const uint2*>(box0 + j * kTpBoxBytes + off_lo);
         const uint2 rh = *reinterpret_cast<const uint2*>(box0 + j * kTpBoxBytes + off_hi);
