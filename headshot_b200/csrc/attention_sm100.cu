@@ -18,7 +18,11 @@
 // tiles, one per softmax warpgroup, against every 96-key K/V tile of that
 // sequence.  Items go out in sequence-major order, so the CTAs working at
 // one time share a few sequences' K/V in L2, and a CTA that runs ahead
-// simply takes more items (no tail from a fixed assignment).
+// simply takes more items (no tail from a fixed assignment).  When one
+// sequence's K and V outgrow a fraction of L2, consecutive waves of items
+// (one item per CTA) walk the K/V tiles in alternating directions, so a wave
+// starts on the tiles the one before it has just read (274,800 keys: DRAM
+// reads 7.5 GB per launch instead of 15.7).
 //
 //   warps 0-3   softmax warpgroup 0 (one thread per query row)
 //   warps 4-7   softmax warpgroup 1
@@ -87,7 +91,8 @@ __host__ __device__ constexpr uint32_t col_s(int wg, int buf) { return static_ca
 __host__ __device__ constexpr uint32_t col_o(int wg) { return static_cast<uint32_t>(4 * kBN + 64 * wg); }
 static_assert(4 * kBN + 2 * 64 <= 512, "TMEM budget");
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: p <= 2^8 between rescales
-constexpr int kEmuPer8 = 2;                // of every 8 exponential pairs, this many run on the FMA pipe
+constexpr int kEmuPer8 = 2;
+constexpr uint64_t kSerpentineKvBytes = 24ull << 20;  // K+V bytes of one sequence above which waves alternate direction                // of every 8 exponential pairs, this many run on the FMA pipe
 
 // Site codes written to the status word when a bounded wait gives up.
 enum : int {
@@ -124,6 +129,7 @@ struct Ctrl {
   uint64_t item_empty[kItemSlots];  // every reader took it
   uint32_t item_seq[kItemSlots];    // decoded item: sequence s*heads+h (kNoItem: no more work)
   uint32_t item_row0[kItemSlots];   // first query row of the item
+  uint32_t item_rev[kItemSlots];    // K/V walk direction of the item
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -154,16 +160,19 @@ struct Args {
   int* status;
   uint32_t* sched;  // [0] items handed out beyond the first gridDim.x, [1] CTAs finished
   uint64_t timeout_ns;
+  uint32_t serp_wave;  // 0: every item walks K/V forward; else item i walks it backward when (i / serp_wave) is odd
 };
 
 struct Item {
-  uint32_t seq;   // s * heads + h
-  uint32_t row0;  // first query row of the item
+  uint32_t seq;       // s * heads + h
+  uint32_t row0;      // first query row of the item
+  uint32_t rev = 0;   // 1: the item takes its K/V tiles last to first
 };
 
 __device__ __forceinline__ Item decode_item(const Args& a, uint32_t item) {
   const uint32_t seq = item / a.pairs;
-  return Item{seq, (item - seq * a.pairs) * kItemRows};
+  const uint32_t rev = a.serp_wave ? (item / a.serp_wave) & 1u : 0u;
+  return Item{seq, (item - seq * a.pairs) * kItemRows, rev};
 }
 
 __device__ __forceinline__ float u2f(uint32_t u) { return __uint_as_float(u); }
@@ -200,6 +209,7 @@ __device__ __forceinline__ bool next_item(const Args& a, Ctrl* ctl, uint32_t k, 
     return false;
   item->seq = *reinterpret_cast<volatile uint32_t*>(&ctl->item_seq[slot]);
   item->row0 = *reinterpret_cast<volatile uint32_t*>(&ctl->item_row0[slot]);
+  item->rev = *reinterpret_cast<volatile uint32_t*>(&ctl->item_rev[slot]);
   __syncwarp();
   if ((threadIdx.x & 31) == 0) mbar_arrive(&ctl->item_empty[slot]);
   return true;
@@ -329,7 +339,7 @@ __device__ void softmax_role(const Args& a, Ctrl* ctl, uint32_t tmem, int warp, 
       tmem_ld32(tS + 32, s + 32);
       tmem_ld32(tS + 64, s + 64);
       tmem_wait_ld_regs<kBN>(s);
-      if (j == n - 1 && tail < kBN) {
+      if (j == (it.rev ? 0u : n - 1) && tail < kBN) {
 #pragma unroll
         for (int i = 0; i < kBN; ++i)
           if (static_cast<uint32_t>(i) >= tail) s[i] = __float_as_uint(-INFINITY);
@@ -499,6 +509,7 @@ __device__ void producer_role(const Args& a, const CUtensorMap* tm_q, const CUte
     const Item it = item < a.n_items ? decode_item(a, item) : Item{kNoItem, 0};
     ctl->item_seq[slot] = it.seq;
     ctl->item_row0[slot] = it.row0;
+    ctl->item_rev[slot] = it.rev;
     mbar_arrive(&ctl->item_full[slot]);  // release: the item is visible to the readers' acquire
     if (it.seq == kNoItem) break;
     item = gridDim.x + atomicAdd(a.sched, 1u);  // used one item later: the latency hides behind the loads
@@ -527,9 +538,10 @@ __device__ void producer_role(const Args& a, const CUtensorMap* tm_q, const CUte
         ok = false;
         break;
       }
+      const int key0 = static_cast<int>((it.rev ? a.n_kv - 1 - j : j) * kBN);
       mbar_arrive_expect_tx(&ctl->kv_full[st], 2 * kKvTileBytes);
-      tma_load_4d(tm_k, &ctl->kv_full[st], sK + st * kKvTileBytes, 0, static_cast<int>(j * kBN), hh, ss);
-      tma_load_4d(tm_v, &ctl->kv_full[st], sV + st * kKvTileBytes, 0, static_cast<int>(j * kBN), hh, ss);
+      tma_load_4d(tm_k, &ctl->kv_full[st], sK + st * kKvTileBytes, 0, key0, hh, ss);
+      tma_load_4d(tm_v, &ctl->kv_full[st], sV + st * kKvTileBytes, 0, key0, hh, ss);
     }
   }
   // Let every load this thread issued land before the CTA can exit (on the
@@ -829,6 +841,11 @@ cudaError_t launch_attention_sm100(cudaStream_t stream, int elem, const AttnIO& 
   a.timeout_ns = timeout_ns;
   uint32_t ctas = max_ctas ? max_ctas : static_cast<uint32_t>(sm_count_of_current_device());
   if (ctas > a.n_items) ctas = a.n_items;
+  // A sequence whose K and V outgrow a fraction of L2: the CTAs that start
+  // items at about the same time (one wave of `ctas` items) stream its K/V
+  // together, and alternate waves walk it in opposite directions, so a wave
+  // starts on the tiles the previous one has just brought into L2.
+  if (static_cast<uint64_t>(a.n_kv) * 2 * kKvTileBytes > kSerpentineKvBytes) a.serp_wave = ctas;
   return bf16 ? launch_typed<__nv_bfloat16>(stream, mq, mk, mv, a, ctas)
               : launch_typed<__half>(stream, mq, mk, mv, a, ctas);
 }

@@ -355,6 +355,30 @@ def test_repeated_calls_are_bit_identical(gpu_ctx, dtype):
         assert torch.equal(first, again), f"call {i + 1} differs from the first"
 
 
+def test_long_sequence_alternating_kv_direction(gpu_ctx):
+    # Past 1024 key tiles (24 MiB of K and V per sequence) every other wave of
+    # items walks K/V last tile to first, so the partial last tile (67 keys
+    # here) is the first one such an item masks.  Rows from forward and
+    # backward items against the oracle over all keys, and the order is a
+    # function of the item index alone: repeated calls agree bit for bit.
+    s, h, t = 1, 2, 100_003
+    rng = np.random.default_rng(77)
+    q, k, v = (rounded(rng.standard_normal((s, h, t, 64), np.float32), "bf16") for _ in range(3))
+    qd, kd, vd = (dev(x, "bf16") for x in (q, k, v))
+    out = gpu_ctx.attention(qd, kd, vd)
+    again = gpu_ctx.attention(qd, kd, vd)
+    gpu_ctx.sync()
+    assert torch.equal(out, again)
+    items = -(-t // 256)
+    # first rows of items in waves 0, 1 and 2 of 148 (head 0) and of head 1's first item, plus random rows
+    starts = [0, 147 * 256, 148 * 256, 295 * 256, 296 * 256, (items - 1) * 256, t + 0, t + 200 * 256]
+    rows = {r + d for r in starts for d in (0, 5, 128, 255) if (r % t) + d < t}
+    rows |= {int(x) for x in rng.integers(0, s * h * t, 256)}
+    rows = np.array(sorted(rows), np.int64)
+    ours = host(out.reshape(-1, 64)[torch.from_numpy(rows).cuda()])
+    gate(ours, oracle.attention_rows(q, k, v, rows))
+
+
 # ---- BASELINE configurations at their own sizes (sampled query rows) --------
 #
 # The bench's workloads, generated exactly as bench.py generates them on rank 0
