@@ -355,6 +355,24 @@ def test_repeated_calls_are_bit_identical(gpu_ctx, dtype):
         assert torch.equal(first, again), f"call {i + 1} differs from the first"
 
 
+@pytest.mark.parametrize("s,h,t", [
+    (1, 3, 1374),  # frames' 94-row last tiles, odd sequence count: the last sequence keeps its own item
+    (2, 16, 100),  # one tile per sequence: every item packs two whole sequences
+    (1, 4, 128),   # last tile exactly 128 rows
+    (1, 2, 129),   # 129 rows: not packed
+    (1, 5, 300),
+    (1, 1, 1374),  # a single sequence: not packed
+])
+def test_packed_last_tiles(gpu_ctx, s, h, t):
+    # Sequences whose last 256-row item has at most 128 rows share items in
+    # pairs (one last tile per warpgroup, two interleaved K/V streams).
+    rng = np.random.default_rng(s * 1000 + h * 10 + t)
+    q, k, v = (rounded(rng.standard_normal((s, h, t, 64), np.float32), "bf16") for _ in range(3))
+    out = gpu_ctx.attention(*(dev(x, "bf16") for x in (q, k, v)))
+    gpu_ctx.sync()
+    gate(host(out), oracle.attention(q, k, v))
+
+
 def test_long_sequence_alternating_kv_direction(gpu_ctx):
     # Past 1024 key tiles (24 MiB of K and V per sequence) every other wave of
     # items walks K/V last tile to first, so the partial last tile (67 keys

@@ -18,7 +18,7 @@ def test_traffic_reported_only_for_the_captured_sources(monkeypatch):
     monkeypatch.setitem(bench.MEASURED_TRAFFIC, "global", {"bytes": 123.0, "sources_sha256": "0" * 64})
     traffic, note = bench.measured_traffic("global")
     assert traffic is None and note.startswith("stale")
-    assert bench.measured_traffic("frame") == (None, "not captured for this workload")
+    assert bench.measured_traffic("block_pair") == (None, "not captured for this workload")
 
 
 def test_aggregator_layouts():
