@@ -104,9 +104,9 @@ WORKLOADS = {
 # the attention kernel's sources at capture time: a figure whose hash no longer
 # matches the sources is not reported (traffic null, with the reason).
 MEASURED_TRAFFIC = {
-    "global": {"bytes": 6594758656 + 574463232, "sources_sha256": "af3726f0864fa3b76e42f0981a36f2282fcc61f0aa3574d1f48b185178e9e8db"},
-    "global43k": {"bytes": 270385152 + 73288192, "sources_sha256": "af3726f0864fa3b76e42f0981a36f2282fcc61f0aa3574d1f48b185178e9e8db"},
-    "frame": {"bytes": 1688943104 + 542603264, "sources_sha256": "af3726f0864fa3b76e42f0981a36f2282fcc61f0aa3574d1f48b185178e9e8db"},
+    "global": {"bytes": 6957943552 + 576583936, "sources_sha256": "845b00488f5fe5b6f2e0542294df6f33b811aae0deccb2ce83b20efa91ef5598"},
+    "global43k": {"bytes": 270670336 + 73345536, "sources_sha256": "845b00488f5fe5b6f2e0542294df6f33b811aae0deccb2ce83b20efa91ef5598"},
+    "frame": {"bytes": 1688890368 + 542964992, "sources_sha256": "845b00488f5fe5b6f2e0542294df6f33b811aae0deccb2ce83b20efa91ef5598"},
 }
 TRAFFIC_SOURCES = ("headshot_b200/csrc/attention_sm100.cu", "headshot_b200/csrc/hs_ptx.cuh")
 

@@ -22,11 +22,7 @@
 // sequence's K and V outgrow a fraction of L2, consecutive waves of items
 // (one item per CTA) walk the K/V tiles in alternating directions, so a wave
 // starts on the tiles the one before it has just read (274,800 keys: DRAM
-// reads 7.0 GB per launch instead of 15.7).  When a sequence's last item has
-// at most 128 rows (frames: 1374 = 5 x 256 + 94), the launch is instantiated
-// with packing: the last tiles of sequences 2p and 2p+1 share one item, one
-// per warpgroup, with two interleaved K/V streams, instead of two items whose
-// second warpgroup idles (outputs bit-identical to the unpacked schedule).
+// reads 7.5 GB per launch instead of 15.7).
 //
 //   warps 0-3   softmax warpgroup 0 (one thread per query row)
 //   warps 4-7   softmax warpgroup 1
@@ -133,7 +129,7 @@ struct Ctrl {
   uint64_t item_empty[kItemSlots];  // every reader took it
   uint32_t item_seq[kItemSlots];    // decoded item: sequence s*heads+h (kNoItem: no more work)
   uint32_t item_row0[kItemSlots];   // first query row of the item
-  uint32_t item_flags[kItemSlots];  // kItemRev | kItemPacked
+  uint32_t item_rev[kItemSlots];    // K/V walk direction of the item
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -165,51 +161,17 @@ struct Args {
   uint32_t* sched;  // [0] items handed out beyond the first gridDim.x, [1] CTAs finished
   uint64_t timeout_ns;
   uint32_t serp_wave;  // 0: every item walks K/V forward; else item i walks it backward when (i / serp_wave) is odd
-  uint32_t pack_pairs;  // packed launches: sequence pairs (2p, 2p+1) whose short last items share one item
 };
-
-// Item flags: the K/V walk direction, and whether the item is packed (its two
-// 128-row tiles are the short last tiles of sequences seq and seq + 1, both
-// starting at row0, with their K/V tiles as two interleaved streams).
-constexpr uint32_t kItemRev = 1u;
-constexpr uint32_t kItemPacked = 2u;
 
 struct Item {
-  uint32_t seq;        // s * heads + h
-  uint32_t row0;       // first query row of the item
-  uint32_t flags = 0;  // kItemRev | kItemPacked
+  uint32_t seq;       // s * heads + h
+  uint32_t row0;      // first query row of the item
+  uint32_t rev = 0;   // 1: the item takes its K/V tiles last to first
 };
 
-// Warpgroup wg's tile of an item: its sequence and first row.
-template <bool kPack>
-__device__ __forceinline__ void wg_tile(const Item& it, int wg, uint32_t* seq, uint32_t* tile0) {
-  *seq = it.seq;
-  *tile0 = it.row0 + wg * kBM;
-  if constexpr (kPack) {
-    if (it.flags & kItemPacked) {
-      *seq = it.seq + wg;
-      *tile0 = it.row0;
-    }
-  }
-}
-
-// Item index -> item.  Sequence-major, `pairs` items per sequence; in a
-// packed launch, per sequence pair the full items of 2p, those of 2p+1, then
-// one packed item with both last tiles (an odd last sequence keeps its own).
-template <bool kPack>
 __device__ __forceinline__ Item decode_item(const Args& a, uint32_t item) {
-  const uint32_t rev = a.serp_wave ? (item / a.serp_wave) & 1u : 0u;
-  if constexpr (kPack) {
-    const uint32_t full = a.pairs - 1;
-    const uint32_t per = 2 * full + 1;
-    const uint32_t p = item / per;
-    const uint32_t r = item - p * per;
-    if (p >= a.pack_pairs) return Item{2 * p, r * kItemRows, rev};
-    if (r == 2 * full) return Item{2 * p, full * kItemRows, rev | kItemPacked};
-    const uint32_t second = r >= full ? 1u : 0u;
-    return Item{2 * p + second, (r - second * full) * kItemRows, rev};
-  }
   const uint32_t seq = item / a.pairs;
+  const uint32_t rev = a.serp_wave ? (item / a.serp_wave) & 1u : 0u;
   return Item{seq, (item - seq * a.pairs) * kItemRows, rev};
 }
 
@@ -247,7 +209,7 @@ __device__ __forceinline__ bool next_item(const Args& a, Ctrl* ctl, uint32_t k, 
     return false;
   item->seq = *reinterpret_cast<volatile uint32_t*>(&ctl->item_seq[slot]);
   item->row0 = *reinterpret_cast<volatile uint32_t*>(&ctl->item_row0[slot]);
-  item->flags = *reinterpret_cast<volatile uint32_t*>(&ctl->item_flags[slot]);
+  item->rev = *reinterpret_cast<volatile uint32_t*>(&ctl->item_rev[slot]);
   __syncwarp();
   if ((threadIdx.x & 31) == 0) mbar_arrive(&ctl->item_empty[slot]);
   return true;
@@ -301,7 +263,7 @@ __device__ __forceinline__ void exp2_poly2(float x0, float x1, float& y0, float&
 // kFixed: every score is known to be bounded (Cauchy-Schwarz on the stored
 // q' and k' rows), so P = 2^(s*c - m_fixed) for a fixed offset m_fixed
 // stays inside the 16-bit type's normal range: no row max, no rescale.
-template <typename E, bool kFixed, bool kPack>
+template <typename E, bool kFixed>
 __device__ void softmax_role(const Args& a, Ctrl* ctl, uint32_t tmem, int warp, int lane, float m_fixed) {
   const int wg = warp >> 2;
   const int wq = warp & 3;
@@ -332,13 +294,12 @@ __device__ void softmax_role(const Args& a, Ctrl* ctl, uint32_t tmem, int warp, 
       return;
     }
     if (it.seq == kNoItem) break;
-    uint32_t seq, tile0;
-    wg_tile<kPack>(it, wg, &seq, &tile0);
+    const uint32_t tile0 = it.row0 + wg * kBM;
     if (tile0 >= a.t_q) continue;  // this warpgroup has no rows in the item
     const uint32_t token = tile0 + row;
     const bool valid = token < a.t_q;
-    const uint64_t row_index = static_cast<uint64_t>(seq) * a.t_q + token;  // head-major (state arrays)
-    const uint64_t out_index = a.lo.at(seq / a.heads, seq % a.heads, token);
+    const uint64_t row_index = static_cast<uint64_t>(it.seq) * a.t_q + token;  // head-major (state arrays)
+    const uint64_t out_index = a.lo.at(it.seq / a.heads, it.seq % a.heads, token);
 
     float m_run = kFixed ? m_fixed : -INFINITY, l = 0.f;
     bool have_o = false;
@@ -378,7 +339,7 @@ __device__ void softmax_role(const Args& a, Ctrl* ctl, uint32_t tmem, int warp, 
       tmem_ld32(tS + 32, s + 32);
       tmem_ld32(tS + 64, s + 64);
       tmem_wait_ld_regs<kBN>(s);
-      if (j == ((it.flags & kItemRev) ? 0u : n - 1) && tail < kBN) {
+      if (j == (it.rev ? 0u : n - 1) && tail < kBN) {
 #pragma unroll
         for (int i = 0; i < kBN; ++i)
           if (static_cast<uint32_t>(i) >= tail) s[i] = __float_as_uint(-INFINITY);
@@ -516,7 +477,7 @@ __host__ __device__ constexpr float fixed_offset_limit() { return Elem<E>::kBf16
 template <typename E>
 __host__ __device__ constexpr float fixed_offset_headroom() { return Elem<E>::kBf16 ? 0.f : 15.5f; }
 
-template <typename E, bool kPack>
+template <typename E>
 __device__ void softmax_dispatch(const Args& a, Ctrl* ctl, uint32_t tmem, int warp, int lane) {
   float bound = INFINITY;
   if (a.qk_norm2 && (a.norm2_shared || (!a.st.load && !a.st.store))) {
@@ -526,14 +487,13 @@ __device__ void softmax_dispatch(const Args& a, Ctrl* ctl, uint32_t tmem, int wa
     bound = qn * kn * a.scale_log2 * 1.0009765625f + 1e-3f;
   }
   if (bound <= fixed_offset_limit<E>())
-    softmax_role<E, true, kPack>(a, ctl, tmem, warp, lane, bound - fixed_offset_headroom<E>());
+    softmax_role<E, true>(a, ctl, tmem, warp, lane, bound - fixed_offset_headroom<E>());
   else
-    softmax_role<E, false, kPack>(a, ctl, tmem, warp, lane, 0.f);
+    softmax_role<E, false>(a, ctl, tmem, warp, lane, 0.f);
 }
 
 // One thread.  Per item: the Q tiles of the warpgroups with rows in it, then
 // the item's K/V tiles through the stage ring.
-template <bool kPack>
 __device__ void producer_role(const Args& a, const CUtensorMap* tm_q, const CUtensorMap* tm_k,
                               const CUtensorMap* tm_v, uint8_t* sQ, uint8_t* sK, uint8_t* sV, Ctrl* ctl) {
   volatile int* abort_flag = &ctl->abort_flag;
@@ -546,17 +506,16 @@ __device__ void producer_role(const Args& a, const CUtensorMap* tm_q, const CUte
     if (k >= kItemSlots && !mbar_wait(&ctl->item_empty[slot], ((k / kItemSlots) - 1) & 1, abort_flag, a.status,
                                       kSiteItemEmpty, a.timeout_ns))
       break;
-    const Item it = item < a.n_items ? decode_item<kPack>(a, item) : Item{kNoItem, 0};
+    const Item it = item < a.n_items ? decode_item(a, item) : Item{kNoItem, 0};
     ctl->item_seq[slot] = it.seq;
     ctl->item_row0[slot] = it.row0;
-    ctl->item_flags[slot] = it.flags;
+    ctl->item_rev[slot] = it.rev;
     mbar_arrive(&ctl->item_full[slot]);  // release: the item is visible to the readers' acquire
     if (it.seq == kNoItem) break;
     item = gridDim.x + atomicAdd(a.sched, 1u);  // used one item later: the latency hides behind the loads
 #pragma unroll
     for (int wg = 0; wg < 2; ++wg) {
-      uint32_t seq, tile0;
-      wg_tile<kPack>(it, wg, &seq, &tile0);
+      const uint32_t tile0 = it.row0 + wg * kBM;
       if (!ok || tile0 >= a.t_q) continue;
       const uint32_t qi = q_issued[wg];
       const uint32_t qb = qi % kQBufs;
@@ -567,28 +526,8 @@ __device__ void producer_role(const Args& a, const CUtensorMap* tm_q, const CUte
       }
       mbar_arrive_expect_tx(&ctl->q_full[wg][qb], kQTileBytes);
       tma_load_4d(tm_q, &ctl->q_full[wg][qb], sQ + (wg * kQBufs + qb) * kQTileBytes, 0, static_cast<int>(tile0),
-                  static_cast<int>(seq % a.heads), static_cast<int>(seq / a.heads));
+                  static_cast<int>(it.seq % a.heads), static_cast<int>(it.seq / a.heads));
       q_issued[wg] = qi + 1;
-    }
-    if constexpr (kPack) {
-      if (it.flags & kItemPacked) {  // two interleaved K/V streams: A0 B0 A1 B1 ...
-        for (uint32_t x = 0; ok && x < 2 * a.n_kv; ++x, ++g) {
-          const uint32_t st = g % kStages;
-          if (g >= kStages &&
-              !mbar_wait(&ctl->kv_empty[st], ((g / kStages) - 1) & 1, abort_flag, a.status, kSiteKvEmpty,
-                         a.timeout_ns)) {
-            ok = false;
-            break;
-          }
-          const uint32_t sq = it.seq + (x & 1u);
-          const int key0 = static_cast<int>((x >> 1) * kBN);
-          const int hh = static_cast<int>(sq % a.heads), ss = static_cast<int>(sq / a.heads);
-          mbar_arrive_expect_tx(&ctl->kv_full[st], 2 * kKvTileBytes);
-          tma_load_4d(tm_k, &ctl->kv_full[st], sK + st * kKvTileBytes, 0, key0, hh, ss);
-          tma_load_4d(tm_v, &ctl->kv_full[st], sV + st * kKvTileBytes, 0, key0, hh, ss);
-        }
-        continue;
-      }
     }
     const int hh = static_cast<int>(it.seq % a.heads), ss = static_cast<int>(it.seq / a.heads);
     for (uint32_t j = 0; ok && j < a.n_kv; ++j, ++g) {
@@ -599,7 +538,7 @@ __device__ void producer_role(const Args& a, const CUtensorMap* tm_q, const CUte
         ok = false;
         break;
       }
-      const int key0 = static_cast<int>(((it.flags & kItemRev) ? a.n_kv - 1 - j : j) * kBN);
+      const int key0 = static_cast<int>((it.rev ? a.n_kv - 1 - j : j) * kBN);
       mbar_arrive_expect_tx(&ctl->kv_full[st], 2 * kKvTileBytes);
       tma_load_4d(tm_k, &ctl->kv_full[st], sK + st * kKvTileBytes, 0, key0, hh, ss);
       tma_load_4d(tm_v, &ctl->kv_full[st], sV + st * kKvTileBytes, 0, key0, hh, ss);
@@ -620,7 +559,7 @@ __device__ void producer_role(const Args& a, const CUtensorMap* tm_q, const CUte
 
 // One MMA warp per softmax warpgroup, all 32 lanes: waits and descriptor
 // math stay warp-uniform and elect.sync picks the lane that issues.
-template <typename E, bool kPack>
+template <typename E>
 __device__ void mma_role(const Args& a, int wg, uint8_t* sQ, uint8_t* sK, uint8_t* sV, Ctrl* ctl, uint32_t tmem) {
   volatile int* abort_flag = &ctl->abort_flag;
   constexpr bool kBf16 = Elem<E>::kBf16;
@@ -681,9 +620,7 @@ __device__ void mma_role(const Args& a, int wg, uint8_t* sQ, uint8_t* sK, uint8_
       break;
     }
     if (it.seq == kNoItem) break;
-    uint32_t it_seq, it_tile0;
-    wg_tile<kPack>(it, wg, &it_seq, &it_tile0);
-    if (it_tile0 >= a.t_q) {
+    if (it.row0 + wg * kBM >= a.t_q) {
       // No rows for this warpgroup: release each stage once it has landed
       // (waiting keeps this warp's view of the ring phases exact).
       for (uint32_t j = 0; j < n; ++j, s_pos.next()) {
@@ -696,21 +633,6 @@ __device__ void mma_role(const Args& a, int wg, uint8_t* sQ, uint8_t* sK, uint8_
       pv_pos = s_pos;
       continue;
     }
-    // A packed item's ring positions alternate between the two warpgroups'
-    // streams: this warp's tile j sits at 2j + wg, and it releases each of the
-    // other stream's stages once it has landed (one arrival, as for an idle
-    // warpgroup), in ring order, so every stage still gets both arrivals.
-    const bool pk = kPack && (it.flags & kItemPacked) != 0;
-    auto skip_other = [&]() {
-      if (!kv_wait(s_pos)) return false;
-      mbar_arrive_elect(&ctl->kv_empty[s_pos.stage]);
-      s_pos.next();
-      return true;
-    };
-    if (pk && wg == 1) {
-      if (!skip_other()) break;
-      pv_pos = s_pos;
-    }
     const uint32_t qb = q_used % kQBufs;
     if (!warp_wait(&ctl->q_full[wg][qb], (q_used / kQBufs) & 1, abort_flag, a.status, kSiteQFull, a.timeout_ns))
       break;
@@ -718,10 +640,6 @@ __device__ void mma_role(const Args& a, int wg, uint8_t* sQ, uint8_t* sK, uint8_
     const uint64_t q_desc = q_desc0 + qb * kQTileStep;
     // S(0) and S(1) up front.  The commit after the item's last S also frees its Q buffer.
     for (uint32_t t = 0; t < 2 && t < n; ++t) {
-      if (pk && t == 1 && !skip_other()) {
-        ok = false;
-        break;
-      }
       if (!kv_wait(s_pos)) {
         ok = false;
         break;
@@ -738,7 +656,6 @@ __device__ void mma_role(const Args& a, int wg, uint8_t* sQ, uint8_t* sK, uint8_
       const int b = static_cast<int>(j & 1);
       const uint32_t st = pv_pos.stage;  // V_j: this stage was waited on before S(j) was issued
       pv_pos.next();
-      if (pk) pv_pos.next();
       if (!warp_wait(&ctl->p_full[wg][b], ((b ? p_base1 : p_base0) + (j >> 1)) & 1, abort_flag, a.status,
                      kSitePFull, a.timeout_ns)) {
         ok = false;
@@ -747,7 +664,7 @@ __device__ void mma_role(const Args& a, int wg, uint8_t* sQ, uint8_t* sK, uint8_
       tc_fence_after();
       issue_pv(st, b, j > 0 || acc0);
       if (j + 2 < n) {
-        if ((pk && !skip_other()) || !kv_wait(s_pos)) {
+        if (!kv_wait(s_pos)) {
           ok = false;
           break;
         }
@@ -766,10 +683,6 @@ __device__ void mma_role(const Args& a, int wg, uint8_t* sQ, uint8_t* sK, uint8_
       }
       umma_commit_elect(&ctl->kv_empty[st]);  // the producer may refill this stage
     }
-    if (pk) {
-      if (ok && wg == 0 && !skip_other()) ok = false;  // the other stream's last tile
-      pv_pos = s_pos;
-    }
     p_base0 += (n + 1) >> 1;
     p_base1 += n >> 1;
     ++q_used;
@@ -782,7 +695,7 @@ __device__ void mma_role(const Args& a, int wg, uint8_t* sQ, uint8_t* sK, uint8_
   (void)drained;
 }
 
-template <typename E, bool kPack>
+template <typename E>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_sm100(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const Args a) {
@@ -840,13 +753,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   // without the split, at 384 or 352 threads, measured 4-5 % slower.)
   if (warp < 8) {
     regs_inc<kSoftmaxRegs>();
-    softmax_dispatch<E, kPack>(a, ctl, tmem, warp, lane);
+    softmax_dispatch<E>(a, ctl, tmem, warp, lane);
   } else {
     regs_dec<kControlRegs>();
     if (warp == kProducerWarp) {
-      if (lane == 0) producer_role<kPack>(a, &tm_q, &tm_k, &tm_v, sQ, sK, sV, ctl);
+      if (lane == 0) producer_role(a, &tm_q, &tm_k, &tm_v, sQ, sK, sV, ctl);
     } else if (warp == kMmaWarp0 || warp == kMmaWarp0 + 1) {
-      mma_role<E, kPack>(a, warp - kMmaWarp0, sQ, sK, sV, ctl, tmem);
+      mma_role<E>(a, warp - kMmaWarp0, sQ, sK, sV, ctl, tmem);
     }
   }
   __syncwarp();
@@ -881,13 +794,13 @@ bool make_map(CUtensorMap* map, const void* base, const RowLayout& l, bool bf16,
 
 int sm_count_of_current_device() { return current_sm_count(); }
 
-template <typename E, bool kPack>
+template <typename E>
 cudaError_t launch_typed(cudaStream_t stream, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                          const Args& a, uint32_t ctas) {
   const cudaError_t e =
-      ensure_dynamic_smem(reinterpret_cast<const void*>(attn_fwd_sm100<E, kPack>), static_cast<int>(kSmemBytes));
+      ensure_dynamic_smem(reinterpret_cast<const void*>(attn_fwd_sm100<E>), static_cast<int>(kSmemBytes));
   if (e != cudaSuccess) return e;
-  attn_fwd_sm100<E, kPack><<<ctas, kThreads, kSmemBytes, stream>>>(mq, mk, mv, a);
+  attn_fwd_sm100<E><<<ctas, kThreads, kSmemBytes, stream>>>(mq, mk, mv, a);
   return cudaGetLastError();
 }
 
@@ -912,13 +825,7 @@ cudaError_t launch_attention_sm100(cudaStream_t stream, int elem, const AttnIO& 
   a.t_kv = t_kv;
   a.n_kv = (t_kv + kBN - 1) / kBN;
   a.pairs = (t_q + kItemRows - 1) / kItemRows;
-  const bool serpentine = static_cast<uint64_t>(a.n_kv) * 2 * kKvTileBytes > kSerpentineKvBytes;
-  // Short last items (at most 128 rows, so one warpgroup would idle through
-  // them): pair the sequences and let one item carry both last tiles.
-  const uint32_t last_rows = t_q - (a.pairs - 1) * kItemRows;
-  if (!serpentine && sh >= 2 && a.n_kv >= 2 && last_rows <= static_cast<uint32_t>(kBM)) a.pack_pairs = sh / 2;
-  const uint64_t items = a.pack_pairs ? static_cast<uint64_t>(a.pack_pairs) * (2 * a.pairs - 1) + (sh & 1u) * a.pairs
-                                      : static_cast<uint64_t>(sh) * a.pairs;
+  const uint64_t items = static_cast<uint64_t>(sh) * a.pairs;
   if (items > 0x7fffffffull) {
     if (err) *err = "too many work items";
     return cudaErrorInvalidValue;
@@ -938,12 +845,9 @@ cudaError_t launch_attention_sm100(cudaStream_t stream, int elem, const AttnIO& 
   // items at about the same time (one wave of `ctas` items) stream its K/V
   // together, and alternate waves walk it in opposite directions, so a wave
   // starts on the tiles the previous one has just brought into L2.
-  if (serpentine) a.serp_wave = ctas;
-  if (a.pack_pairs)
-    return bf16 ? launch_typed<__nv_bfloat16, true>(stream, mq, mk, mv, a, ctas)
-                : launch_typed<__half, true>(stream, mq, mk, mv, a, ctas);
-  return bf16 ? launch_typed<__nv_bfloat16, false>(stream, mq, mk, mv, a, ctas)
-              : launch_typed<__half, false>(stream, mq, mk, mv, a, ctas);
+  if (static_cast<uint64_t>(a.n_kv) * 2 * kKvTileBytes > kSerpentineKvBytes) a.serp_wave = ctas;
+  return bf16 ? launch_typed<__nv_bfloat16>(stream, mq, mk, mv, a, ctas)
+              : launch_typed<__half>(stream, mq, mk, mv, a, ctas);
 }
 
 }  // namespace hs

@@ -356,16 +356,16 @@ def test_repeated_calls_are_bit_identical(gpu_ctx, dtype):
 
 
 @pytest.mark.parametrize("s,h,t", [
-    (1, 3, 1374),  # frames' 94-row last tiles, odd sequence count: the last sequence keeps its own item
-    (2, 16, 100),  # one tile per sequence: every item packs two whole sequences
-    (1, 4, 128),   # last tile exactly 128 rows
-    (1, 2, 129),   # 129 rows: not packed
+    (1, 3, 1374),  # frames' 94-row last items (warpgroup 1 idle), odd sequence count
+    (2, 16, 100),  # one short item per sequence
+    (1, 4, 128),   # last item exactly one 128-row tile
+    (1, 2, 129),   # one row into the second tile
     (1, 5, 300),
-    (1, 1, 1374),  # a single sequence: not packed
+    (1, 1, 1374),  # a single sequence
 ])
-def test_packed_last_tiles(gpu_ctx, s, h, t):
-    # Sequences whose last 256-row item has at most 128 rows share items in
-    # pairs (one last tile per warpgroup, two interleaved K/V streams).
+def test_short_last_items(gpu_ctx, s, h, t):
+    # Items whose second 128-row tile lies past the sequence end: that
+    # warpgroup and its MMA warp skip the item and only release its K/V stages.
     rng = np.random.default_rng(s * 1000 + h * 10 + t)
     q, k, v = (rounded(rng.standard_normal((s, h, t, 64), np.float32), "bf16") for _ in range(3))
     out = gpu_ctx.attention(*(dev(x, "bf16") for x in (q, k, v)))
