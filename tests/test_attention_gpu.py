@@ -71,9 +71,9 @@ def test_attention_tails_bf16(gpu_ctx, t):
 def test_attention_running_max_jump(gpu_ctx, dtype, jump):
     # Key 530 (tile 5 of 96-key tiles) scores `jump` log2 units above what
     # any query saw before, so the running max moves past the lazy-rescale
-    # threshold (2^8) in a later tile.  The kernel's cheap test (the tile's
-    # rounded row sum reaching 2^8) must catch it and rebuild the scores;
-    # at 40 the first-pass 16-bit P also overflows (f16) before the rebuild.
+    # threshold (2^8) in a later tile: that tile's row max replaces the
+    # running one and O and l are rescaled before its PV product.  At 40 a P
+    # taken against the old max would overflow f16 (2^40).
     s, h, t, d = 1, 2, 700, 64
     rng = np.random.default_rng(11)
     u = rng.standard_normal(d).astype(np.float32)
