@@ -335,8 +335,10 @@ def run_ours(args, wl: dict, rank: int, world: int, local: int) -> dict | None:
         def step():
             ctx.attention_fused(q, k, v, qk_norm=norm, rope=rope, out=out)
     else:
+        global_call = session.attention_ulysses if args.global_mode == "ulysses" else session.attention_fused
+
         def step():
-            session.attention_fused(q, k, v, out, T_total=T, qk_norm=norm, rope=rope)
+            global_call(q, k, v, out, T_total=T, qk_norm=norm, rope=rope)
 
     stream = torch.cuda.current_stream(dev)
     for _ in range(args.warmup):
@@ -390,7 +392,7 @@ def run_ours(args, wl: dict, rank: int, world: int, local: int) -> dict | None:
         elif session is None:
             ctx.attention_fused(qq, kk, vv, qk_norm=norm, rope=rope, out=oo)
         else:
-            session.attention_fused(qq, kk, vv, oo, T_total=T, qk_norm=norm, rope=rope)
+            global_call(qq, kk, vv, oo, T_total=T, qk_norm=norm, rope=rope)
 
     def e2e_serial():
         ctx.upload(q, qh)
@@ -467,7 +469,12 @@ def run_ours(args, wl: dict, rank: int, world: int, local: int) -> dict | None:
     # ---- roofline of the dominant kernel (attention), live events ----
     peaks = measured_peaks()
     attn_per_launch_ms = attn_ms / max(attn_n, 1)
-    flops_per_launch = flops_rank if session is None else flops_rank / world
+    if session is None:
+        flops_per_launch = flops_rank
+    elif args.global_mode == "ulysses":  # one launch over the whole sequence of H / world heads
+        flops_per_launch = 4.0 * (H // world) * T * T * 64
+    else:  # one ring step: this rank's queries against one block of keys
+        flops_per_launch = flops_rank / world
     achieved = flops_per_launch / (attn_per_launch_ms / 1e3) / 1e12
     # DRAM bytes per attention launch from one-pass ncu captures of these exact
     # single-GPU launches, reported only while the kernel sources still hash to
@@ -493,6 +500,7 @@ def run_ours(args, wl: dict, rank: int, world: int, local: int) -> dict | None:
         # What the step spends outside attention launches is what the transfers, the
         # Q'/K' prep and the launches' own tails did not hide.
         roofline["ring"] = {
+            "mode": args.global_mode,
             "reserved_sms": args.ring_reserved_sms if args.ring_reserved_sms is not None else "library default (0)",
             "transfers_per_step": round(xfer_n / args.steps, 2),
             "transfer_span_ms_per_step": round(xfer_ms / args.steps, 3),
@@ -518,7 +526,8 @@ def run_ours(args, wl: dict, rank: int, world: int, local: int) -> dict | None:
                        "tokens": S * T, "tokens_per_s": round(S * T / (ms_per_step / 1e3), 1),
                        "flops_per_step": flops_total,
                        "frac_of_measured_bf16_peak": round(value / peaks["bf16"], 4),
-                       "parallelism": ("ring sequence-parallel" if S == 1 else "frame-sharded") + f" x{world}",
+                       "parallelism": (("head-parallel all-to-all" if args.global_mode == "ulysses" and world > 1
+                                        else "ring sequence-parallel") if S == 1 else "frame-sharded") + f" x{world}",
                        "l2": "inputs larger than L2 (each of q/k/v > 126 MB); no flush needed"},
             "roofline": roofline,
             "cpu_baseline": cpu,
@@ -1378,6 +1387,8 @@ def main():
     ap.add_argument("--cpu-threads", type=int, default=0)
     ap.add_argument("--ref-step-seconds", type=float, default=4.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--global-mode", choices=["ring", "ulysses"], default="ring",
+                    help="multi-GPU global attention: the K/V ring, or head parallelism by all-to-all")
     ap.add_argument("--ring-reserved-sms", type=int, default=None,
                     help="SMs the ring's attention launches leave to the block transfers (default: the library's)")
     args = ap.parse_args()

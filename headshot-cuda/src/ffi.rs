@@ -91,6 +91,12 @@ unsafe extern "C" {
                                          q_norm_b: *const f32, k_norm_w: *const f32, k_norm_b: *const f32,
                                          eps: f32, rope_sin: *const f32, rope_cos: *const f32, rope_rows: u32,
                                          prefix: u32, tokens_per_frame: u32, shard_unit: u32) -> hs_status;
+    pub fn hs_ring_ulysses_attention_fused(ring: *mut hs_ring, q: *const c_void, k: *const c_void,
+                                           v: *const c_void, out: *mut c_void, h: u32, t_total: u32, d: u32,
+                                           dtype: hs_dtype, scale: f32, q_norm_w: *const f32,
+                                           q_norm_b: *const f32, k_norm_w: *const f32, k_norm_b: *const f32,
+                                           eps: f32, rope_sin: *const f32, rope_cos: *const f32,
+                                           rope_rows: u32, prefix: u32, tokens_per_frame: u32) -> hs_status;
     pub fn hs_ring_set_reserved_sms(ring: *mut hs_ring, sms: u32) -> hs_status;
     pub fn hs_ring_sync(ring: *mut hs_ring, timeout_ms: u32) -> hs_status;
     // trunk glue and host helpers

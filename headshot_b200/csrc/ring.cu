@@ -132,6 +132,13 @@ struct hs_ring {
   // costs attention throughput in proportion; it pays when the transfers are
   // large next to the launches (many ranks, short shards).
   uint32_t reserved_sms = 0;
+  // Head-parallel path (hs_ring_ulysses_attention_fused): this rank's Q' and
+  // K' shards, then Q', K', V and the output of its H / R heads over the whole
+  // sequence; events ordering the two all-to-alls against the attention.
+  uint8_t* uly = nullptr;
+  size_t uly_bytes = 0;
+  cudaEvent_t ev_in = nullptr;   // the inbound all-to-all landed
+  cudaEvent_t ev_attn = nullptr; // the attention over the gathered heads is done
 };
 
 extern "C" {
@@ -190,7 +197,7 @@ hs_status hs_ring_create(hs_ctx* ctx, int rank, int world, const void* id, hs_ri
   }
   cudaError_t e = cudaStreamCreateWithFlags(&ring->comm_stream, cudaStreamNonBlocking);
   for (cudaEvent_t* ev : {&ring->ev_block0, &ring->ev_recv[0], &ring->ev_recv[1], &ring->ev_compute[0],
-                          &ring->ev_compute[1], &ring->ev_done, &ring->ev_bound})
+                          &ring->ev_compute[1], &ring->ev_done, &ring->ev_bound, &ring->ev_in, &ring->ev_attn})
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(ev, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaMalloc(&ring->norm2, 2 * sizeof(unsigned int));
   if (e != cudaSuccess) {
@@ -227,9 +234,10 @@ hs_status hs_ring_destroy(hs_ring* ring) {
   for (void* b : ring->buf)
     if (b) cudaFree(b);
   if (ring->state) cudaFree(ring->state);
+  if (ring->uly) cudaFree(ring->uly);
   if (ring->norm2) cudaFree(ring->norm2);
   for (cudaEvent_t ev : {ring->ev_block0, ring->ev_recv[0], ring->ev_recv[1], ring->ev_compute[0],
-                         ring->ev_compute[1], ring->ev_done, ring->ev_bound})
+                         ring->ev_compute[1], ring->ev_done, ring->ev_bound, ring->ev_in, ring->ev_attn})
     if (ev) cudaEventDestroy(ev);
   if (ring->comm_stream) cudaStreamDestroy(ring->comm_stream);
   delete ring;
@@ -433,6 +441,216 @@ hs_status ring_attention(hs_ring* ring, const void* q, const void* k, const void
   return HS_OK;
 }
 
+// Head-parallel global attention (sequence parallelism by an all-to-all over
+// heads): rank r holds tokens shard(T, R, r) of all H heads, as for the ring.
+// The Q'/K' prep runs on the local shard (global RoPE positions), then one
+// all-to-all gives every rank the whole sequence of its H / R heads, one
+// attention launch computes them with nothing carried between launches, and a
+// second all-to-all returns each rank's tokens of every head.  Per rank it
+// moves 3 (R-1)/R of its q, k, v shard in and (R-1)/R of its output back,
+// against (R-1) K/V blocks for the ring; H must be a multiple of R.
+hs_status ulysses_attention(hs_ring* ring, const void* q, const void* k, const void* v, void* out, uint32_t H,
+                            uint32_t T_total, uint32_t D, hs_dtype dtype, float scale, const float* q_norm_w,
+                            const float* q_norm_b, const float* k_norm_w, const float* k_norm_b, float eps,
+                            const float* rope_sin, const float* rope_cos, uint32_t rope_rows, uint32_t prefix,
+                            uint32_t tokens_per_frame, const char* name) {
+  if (!ring) return hs::abi_fail(HS_ERR_INVALID, std::string(name) + ": null ring");
+  if (ring->aborted) return hs::abi_fail(HS_ERR_NCCL, std::string(name) + ": ring was aborted");
+  hs_ctx* ctx = ring->ctx;
+  const int R = ring->world, r = ring->rank;
+  if (ctx->cancel.load()) return hs::abi_fail(HS_ERR_CANCELLED, std::string(name) + ": cancelled");
+  if (dtype != HS_F16 && dtype != HS_BF16)
+    return hs::abi_fail(HS_ERR_UNSUPPORTED, std::string(name) + ": f16/bf16 storage only");
+  if (D != 64) return hs::abi_fail(HS_ERR_UNSUPPORTED, std::string(name) + ": head_dim must be 64");
+  if (H == 0 || H > 65535 || H % static_cast<uint32_t>(R) != 0)
+    return hs::abi_fail(HS_ERR_INVALID, std::string(name) + ": H must be a positive multiple of the ring size");
+  if (T_total < static_cast<uint32_t>(R))
+    return hs::abi_fail(HS_ERR_INVALID, std::string(name) + ": need one token per rank");
+  if (R == 1)
+    return hs_attention_fused(ctx, q, k, v, out, 1, H, T_total, D, dtype, scale, q_norm_w, q_norm_b, k_norm_w,
+                              k_norm_b, eps, rope_sin, rope_cos, rope_rows, prefix, tokens_per_frame);
+  if (!q || !k || !v || !out) return hs::abi_fail(HS_ERR_INVALID, std::string(name) + ": null tensor pointer");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
+    return hs::abi_fail(HS_ERR_INVALID, std::string(name) + ": tensor pointers must be 16-byte aligned");
+  const bool ln = q_norm_w != nullptr;
+  if (ln != (k_norm_w != nullptr) || (ln && (!q_norm_b || !k_norm_b)))
+    return hs::abi_fail(HS_ERR_INVALID, std::string(name) + ": QK-norm needs all of q/k weight and bias, or none");
+  const bool rope = rope_sin != nullptr;
+  const uint32_t tpf = tokens_per_frame ? tokens_per_frame : T_total;
+  if (rope && (!rope_cos || prefix > tpf || rope_rows < tpf - prefix || !aligned16(rope_sin) || !aligned16(rope_cos)))
+    return hs::abi_fail(HS_ERR_INVALID, std::string(name) + ": bad RoPE tables / prefix");
+  if (!(scale > 0.f) || !isfinite(scale)) scale = 1.0f / sqrtf(static_cast<float>(D));
+
+  cudaSetDevice(ctx->device);
+  NcclApi& n = nccl();
+  cudaStream_t st = hs::ctx_stream(ctx);
+  cudaStream_t cs = ring->comm_stream;
+  const int code = static_cast<int>(dtype);
+  const size_t row_bytes = 64 * 2;
+  const uint32_t G = H / static_cast<uint32_t>(R);  // heads per rank
+  uint32_t t0, tr;
+  shard(T_total, R, r, &t0, &tr);
+  const uint32_t tmax = (T_total + R - 1) / R;
+  const size_t local_rows = static_cast<size_t>(H) * tmax;
+  const size_t full_rows = static_cast<size_t>(G) * T_total;
+  const size_t need = (2 * local_rows + 4 * full_rows) * row_bytes;
+  cudaError_t e;
+  if (ring->uly_bytes < need) {
+    cudaStreamSynchronize(st);
+    cudaStreamSynchronize(cs);
+    if (ring->uly) cudaFree(ring->uly);
+    ring->uly = nullptr;
+    ring->uly_bytes = 0;
+    e = cudaMalloc(&ring->uly, need);
+    if (e != cudaSuccess) return hs::abi_cuda_fail(e, "head-parallel buffers");
+    ring->uly_bytes = need;
+  }
+  uint8_t* lq = ring->uly;                   // (H, tr) Q' of this rank's tokens
+  uint8_t* lk = lq + local_rows * row_bytes;  // (H, tr) K'
+  uint8_t* fq = lk + local_rows * row_bytes;  // (G, T_total) Q' of this rank's heads
+  uint8_t* fk = fq + full_rows * row_bytes;
+  uint8_t* fv = fk + full_rows * row_bytes;
+  uint8_t* fo = fv + full_rows * row_bytes;   // (G, T_total) output of this rank's heads
+
+  // Q' and K' of the local tokens, with global RoPE positions, and their
+  // largest row norms: an all-ranks max bounds every score (fixed offset).
+  const bool bounded = ln || rope;
+  const void* src_q = q;
+  const void* src_k = k;
+  if (bounded) {
+    hs::QkPrologue qp{};
+    qp.ln = ln;
+    qp.ln_w = q_norm_w;
+    qp.ln_b = q_norm_b;
+    qp.eps = eps;
+    qp.rope = rope;
+    qp.sin_t = rope_sin;
+    qp.cos_t = rope_cos;
+    qp.prefix = prefix;
+    qp.tokens_per_frame = tpf;
+    qp.pos_offset = t0;
+    hs::QkPrologue kp = qp;
+    kp.ln_w = k_norm_w;
+    kp.ln_b = k_norm_b;
+    e = cudaMemsetAsync(ring->norm2, 0, 2 * sizeof(unsigned int), st);
+    if (e != cudaSuccess) return hs::abi_cuda_fail(e, "head-parallel bound reset");
+    qp.norm2_max = ring->norm2;
+    kp.norm2_max = ring->norm2 + 1;
+    const hs::RowLayout rows_in = hs::RowLayout::head_major(H, tr);
+    const hs::PrepJob jobs[2] = {{k, rows_in, lk, kp}, {q, rows_in, lq, qp}};
+    {
+      hs::ProfScope prof(ctx, st, "qk_prep");
+      e = hs::launch_qk_prep(st, code, code, 1, H, tr, jobs, 2, ctx->d_status, hs::ctx_timeout_ns(ctx));
+    }
+    if (e != cudaSuccess) return hs::abi_cuda_fail(e, "head-parallel Q'/K' prep");
+    src_q = lq;
+    src_k = lk;
+  }
+  cudaEventRecord(ring->ev_block0, st);
+  cudaStreamWaitEvent(cs, ring->ev_block0, 0);
+  if (bounded) {
+    ncclResult_t nr = n.AllReduce(ring->norm2, ring->norm2, 2, ncclUint32, ncclMax, ring->comm, cs);
+    if (nr != ncclSuccess) return nccl_fail(nr, "head-parallel bound all-reduce");
+  }
+
+  // Inbound all-to-all.  To each rank p this rank sends its rows of head
+  // p*G + j (tr contiguous rows of its head-major (H, tr) shard), which p
+  // stores at rows [t0, t0 + tr) of its head j; from each p it receives p's
+  // rows of head r*G + j into rows [t0_p, t0_p + tr_p) of its own head j.
+  // Every pair issues its sends and receives in the same (tensor, head) order.
+  const void* src[3] = {src_q, src_k, v};
+  uint8_t* dst[3] = {fq, fk, fv};
+  {
+    hs::ProfScope prof(ctx, cs, "ring_transfer");
+    ncclResult_t nr = n.GroupStart();
+    for (int x = 0; x < 3 && nr == ncclSuccess; ++x) {
+      const uint8_t* sx = static_cast<const uint8_t*>(src[x]);
+      for (int p = 0; p < R && nr == ncclSuccess; ++p) {
+        if (p == r) continue;
+        uint32_t p0, pl;
+        shard(T_total, R, p, &p0, &pl);
+        for (uint32_t j = 0; j < G && nr == ncclSuccess; ++j) {
+          const size_t send_row = (static_cast<size_t>(p) * G + j) * tr;
+          nr = n.Send(sx + send_row * row_bytes, static_cast<size_t>(tr) * row_bytes, ncclUint8, p, ring->comm, cs);
+          if (nr != ncclSuccess) break;
+          const size_t recv_row = static_cast<size_t>(j) * T_total + p0;
+          nr = n.Recv(dst[x] + recv_row * row_bytes, static_cast<size_t>(pl) * row_bytes, ncclUint8, p, ring->comm,
+                      cs);
+        }
+      }
+    }
+    ncclResult_t ge = n.GroupEnd();
+    if (nr != ncclSuccess) return nccl_fail(nr, "head-parallel send/recv");
+    if (ge != ncclSuccess) return nccl_fail(ge, "head-parallel group");
+  }
+  // This rank's own rows of its heads.
+  for (int x = 0; x < 3; ++x)
+    for (uint32_t j = 0; j < G; ++j) {
+      const size_t from = (static_cast<size_t>(r) * G + j) * tr, to = static_cast<size_t>(j) * T_total + t0;
+      e = cudaMemcpyAsync(dst[x] + to * row_bytes, static_cast<const uint8_t*>(src[x]) + from * row_bytes,
+                          static_cast<size_t>(tr) * row_bytes, cudaMemcpyDeviceToDevice, cs);
+      if (e != cudaSuccess) return hs::abi_cuda_fail(e, "head-parallel local rows");
+    }
+  cudaEventRecord(ring->ev_in, cs);
+  cudaStreamWaitEvent(st, ring->ev_in, 0);
+
+  // One launch over the whole sequence of this rank's heads.
+  std::string err;
+  {
+    hs::ProfScope prof(ctx, st, "attention");
+    hs::AttnIO io;
+    const hs::RowLayout full = hs::RowLayout::head_major(G, T_total);
+    io.q = fq;
+    io.lq = full;
+    io.k = fk;
+    io.lk = full;
+    io.v = fv;
+    io.lv = full;
+    io.out = fo;
+    io.lo = full;
+    io.out_code = code;
+    e = hs::launch_attention_sm100(st, code, io, 1, G, T_total, T_total, scale, hs::AttnState{}, 0, ctx->d_status,
+                                   ctx->d_sched, bounded ? ring->norm2 : nullptr, true, hs::ctx_timeout_ns(ctx),
+                                   &err);
+  }
+  if (e != cudaSuccess)
+    return hs::abi_fail(HS_ERR_CUDA, std::string(name) + ": " + (err.empty() ? cudaGetErrorString(e) : err));
+  cudaEventRecord(ring->ev_attn, st);
+  cudaStreamWaitEvent(cs, ring->ev_attn, 0);
+
+  // Outbound all-to-all: rows [t0_p, t0_p + tr_p) of each of this rank's heads
+  // go to rank p, which stores them as its head r*G + j.
+  uint8_t* o = static_cast<uint8_t*>(out);
+  {
+    hs::ProfScope prof(ctx, cs, "ring_transfer");
+    ncclResult_t nr = n.GroupStart();
+    for (int p = 0; p < R && nr == ncclSuccess; ++p) {
+      if (p == r) continue;
+      uint32_t p0, pl;
+      shard(T_total, R, p, &p0, &pl);
+      for (uint32_t j = 0; j < G && nr == ncclSuccess; ++j) {
+        const size_t send_row = static_cast<size_t>(j) * T_total + p0;
+        nr = n.Send(fo + send_row * row_bytes, static_cast<size_t>(pl) * row_bytes, ncclUint8, p, ring->comm, cs);
+        if (nr != ncclSuccess) break;
+        const size_t recv_row = (static_cast<size_t>(p) * G + j) * tr;
+        nr = n.Recv(o + recv_row * row_bytes, static_cast<size_t>(tr) * row_bytes, ncclUint8, p, ring->comm, cs);
+      }
+    }
+    ncclResult_t ge = n.GroupEnd();
+    if (nr != ncclSuccess) return nccl_fail(nr, "head-parallel output send/recv");
+    if (ge != ncclSuccess) return nccl_fail(ge, "head-parallel output group");
+  }
+  for (uint32_t j = 0; j < G; ++j) {
+    const size_t from = static_cast<size_t>(j) * T_total + t0, to = (static_cast<size_t>(r) * G + j) * tr;
+    e = cudaMemcpyAsync(o + to * row_bytes, fo + from * row_bytes, static_cast<size_t>(tr) * row_bytes,
+                        cudaMemcpyDeviceToDevice, cs);
+    if (e != cudaSuccess) return hs::abi_cuda_fail(e, "head-parallel local output rows");
+  }
+  cudaEventRecord(ring->ev_done, cs);
+  cudaStreamWaitEvent(st, ring->ev_done, 0);
+  return HS_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -456,6 +674,17 @@ hs_status hs_ring_attention_block_fused(hs_ring* ring, const void* q, const void
   return ring_attention(ring, q, k, v, out, H, T_total, D, dtype, scale, q_norm_w, q_norm_b, k_norm_w, k_norm_b, eps,
                         rope_sin, rope_cos, rope_rows, prefix, tokens_per_frame, true, shard_unit,
                         "hs_ring_attention_block_fused");
+}
+
+hs_status hs_ring_ulysses_attention_fused(hs_ring* ring, const void* q, const void* k, const void* v, void* out,
+                                          uint32_t H, uint32_t T_total, uint32_t D, hs_dtype dtype, float scale,
+                                          const float* q_norm_w, const float* q_norm_b, const float* k_norm_w,
+                                          const float* k_norm_b, float eps, const float* rope_sin,
+                                          const float* rope_cos, uint32_t rope_rows, uint32_t prefix,
+                                          uint32_t tokens_per_frame) {
+  return ulysses_attention(ring, q, k, v, out, H, T_total, D, dtype, scale, q_norm_w, q_norm_b, k_norm_w, k_norm_b,
+                           eps, rope_sin, rope_cos, rope_rows, prefix, tokens_per_frame,
+                           "hs_ring_ulysses_attention_fused");
 }
 
 hs_status hs_ring_sync(hs_ring* ring, uint32_t timeout_ms) {

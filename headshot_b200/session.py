@@ -7,7 +7,10 @@ reference is single-device, src/model/trunk.rs:92-144).
   shard_bounds(T, R, r) of q, k and v (all heads) and runs the ring in
   libheadshot_cuda.so (hs_ring_attention_fused): [K'|V] blocks rotate over
   NCCL send/recv while the tcgen05 kernel works on the previous block,
-  carrying the f32 softmax state in-kernel.
+  carrying the f32 softmax state in-kernel.  Or by head parallelism
+  (hs_ring_ulysses_attention_fused): an all-to-all gives each rank the
+  whole sequence of H / world heads, one attention launch, an all-to-all
+  back.
 
 Failure detection: before each ring call every rank joins a small host
 "preflight" collective on the session's process group; a rank that has
@@ -36,6 +39,8 @@ RING_SIGNATURES = {
                                      _vp, _vp, _u32, _u32, _u32]),
     "hs_ring_attention_block_fused": (_i, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _i, _f32, _vp, _vp, _vp, _vp,
                                            _f32, _vp, _vp, _u32, _u32, _u32, _u32]),
+    "hs_ring_ulysses_attention_fused": (_i, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _i, _f32, _vp, _vp, _vp, _vp,
+                                             _f32, _vp, _vp, _u32, _u32, _u32]),
     "hs_ring_sync": (_i, [_vp, _u32]),
     "hs_ring_set_reserved_sms": (_i, [_vp, _u32]),
 }
@@ -125,6 +130,10 @@ class RingSession:
     def attention_fused(self, q, k, v, out, T_total: int, qk_norm=None, rope=None, scale: float | None = None,
                         check_peers: bool = False):
         """Ring global attention on this rank's shard: q, k, v, out (H, T_r, 64) or (1, H, T_r, 64)."""
+        return self._global(self._L.hs_ring_attention_fused, q, k, v, out, T_total, qk_norm, rope, scale,
+                            check_peers)
+
+    def _global(self, fn, q, k, v, out, T_total, qk_norm, rope, scale, check_peers):
         import torch
 
         from .engine import _code, _ptr
@@ -150,11 +159,18 @@ class RingSession:
             tpf = rope.tokens_per_frame or T_total
         check(self._L.hs_ctx_set_stream(self.ctx.handle,
                                         ctypes.c_void_p(torch.cuda.current_stream(self.ctx.device).cuda_stream)))
-        check(self._L.hs_ring_attention_fused(
-            self._h, _ptr(q), _ptr(k), _ptr(v), _ptr(out), h, T_total, 64, _code(q),
-            0.0 if scale is None else float(scale), *[_ptr(x) for x in n_args], float(eps), _ptr(r_sin), _ptr(r_cos),
-            rows, prefix, tpf))
+        check(fn(self._h, _ptr(q), _ptr(k), _ptr(v), _ptr(out), h, T_total, 64, _code(q),
+                 0.0 if scale is None else float(scale), *[_ptr(x) for x in n_args], float(eps), _ptr(r_sin),
+                 _ptr(r_cos), rows, prefix, tpf))
         return out
+
+    def attention_ulysses(self, q, k, v, out, T_total: int, qk_norm=None, rope=None, scale: float | None = None,
+                          check_peers: bool = False):
+        """attention_fused's contract by head parallelism (hs_ring_ulysses_attention_fused): an
+        all-to-all gathers the whole sequence of H / world heads on each rank, one attention launch,
+        an all-to-all back.  H must be a multiple of the world size."""
+        return self._global(self._L.hs_ring_ulysses_attention_fused, q, k, v, out, T_total, qk_norm, rope, scale,
+                            check_peers)
 
     def unit_shard(self, t_total: int, unit: int) -> tuple[int, int]:
         """Token range of this rank when shards are whole `unit`s of tokens (whole frames)."""

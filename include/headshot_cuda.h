@@ -271,6 +271,20 @@ HS_API hs_status hs_ring_attention_block_fused(hs_ring* ring, const void* q, con
                                                const float* k_norm_b, float eps, const float* rope_sin,
                                                const float* rope_cos, uint32_t rope_rows, uint32_t prefix,
                                                uint32_t tokens_per_frame, uint32_t shard_unit);
+/* hs_ring_attention_fused's contract (each rank's (1, H, T_r, 64) shard of
+ * hs_ring_shard's tokens in and out, global RoPE positions, f16/bf16), by
+ * head parallelism instead of the ring: the Q'/K' prep runs on the local
+ * shard, an all-to-all over NCCL gives each rank the whole sequence of its
+ * H / world heads, one attention launch computes them (no softmax state
+ * carried between launches), and a second all-to-all returns every rank's
+ * tokens of all heads.  H must be a multiple of the ring's world size.  New
+ * (the reference is single-device, src/model/trunk.rs:92-144). */
+HS_API hs_status hs_ring_ulysses_attention_fused(hs_ring* ring, const void* q, const void* k, const void* v,
+                                                 void* out, uint32_t H, uint32_t T_total, uint32_t D, hs_dtype dtype,
+                                                 float scale, const float* q_norm_w, const float* q_norm_b,
+                                                 const float* k_norm_w, const float* k_norm_b, float eps,
+                                                 const float* rope_sin, const float* rope_cos, uint32_t rope_rows,
+                                                 uint32_t prefix, uint32_t tokens_per_frame);
 /* Waits for the ring's work with a host-side watchdog: on an NCCL async
  * error or after timeout_ms the communicator is aborted and the ring
  * becomes unusable (HS_ERR_NCCL / HS_ERR_TIMEOUT). */

@@ -1,7 +1,8 @@
 """One rank of the ring-attention GPU test (spawned by tests/test_ring_gpu.py).
 
 Builds the global seeded inputs, keeps this rank's shard, runs
-RingSession.attention_fused over NCCL and saves the local output."""
+RingSession.attention_fused (or attention_ulysses, the head-parallel
+all-to-all path) over NCCL and saves the local output."""
 from __future__ import annotations
 
 import os
@@ -25,7 +26,7 @@ def device_inputs(dev, T: int, H: int, dtype: str, seed: int):
 
 
 def run(rank: int, world: int, port: int, outdir: str, T: int, H: int, dtype: str, seed: int, fused: bool,
-        unit: int = 0, gen: str = "np") -> None:
+        unit: int = 0, gen: str = "np", mode: str = "ring") -> None:
     """unit = 0: head-major (1, H, T_r, 64) shards of hs_shard's token rule (attention_fused);
     unit > 0: the (T_r, H*64) projection layout in shards of whole `unit`-token frames
     (attention_block).  gen = "np": inputs from numpy's generator (small cases); "torch":
@@ -80,8 +81,8 @@ def run(rank: int, world: int, port: int, outdir: str, T: int, H: int, dtype: st
                 sess.attention_block(loc(q), loc(k), loc(v), out, T_total=T, heads=H, shard_unit=unit,
                                      qk_norm=norm, rope=rope, check_peers=True)
             else:
-                sess.attention_fused(loc(q), loc(k), loc(v), out, T_total=T, qk_norm=norm, rope=rope,
-                                     check_peers=True)
+                call = sess.attention_ulysses if mode == "ulysses" else sess.attention_fused
+                call(loc(q), loc(k), loc(v), out, T_total=T, qk_norm=norm, rope=rope, check_peers=True)
             sess.sync(60_000)
         np.save(Path(outdir) / f"out_{rank}.npy", out.float().cpu().numpy())
         sess.close()
@@ -93,4 +94,4 @@ def run(rank: int, world: int, port: int, outdir: str, T: int, H: int, dtype: st
 if __name__ == "__main__":
     a = sys.argv[1:]
     run(int(a[0]), int(a[1]), int(a[2]), a[3], int(a[4]), int(a[5]), a[6], int(a[7]), a[8] == "1",
-        int(a[9]) if len(a) > 9 else 0, a[10] if len(a) > 10 else "np")
+        int(a[9]) if len(a) > 9 else 0, a[10] if len(a) > 10 else "np", a[11] if len(a) > 11 else "ring")

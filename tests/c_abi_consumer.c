@@ -46,6 +46,7 @@ static const any_fn entry_points[] = {
     FN(hs_ring_create),           FN(hs_ring_destroy),
     FN(hs_ring_attention_fused),  FN(hs_ring_attention_block_fused),
     FN(hs_ring_sync),             FN(hs_ring_set_reserved_sms),
+    FN(hs_ring_ulysses_attention_fused),
     FN(hs_copy_row_blocks),
     FN(hs_im2col_patch),          FN(hs_cache_build),
     FN(hs_rope_periods),          FN(hs_rope_tables),

@@ -1,4 +1,5 @@
-"""Ring (sequence-parallel) global attention on 2+ GPUs against the oracle.
+"""Ring (sequence-parallel) and head-parallel (all-to-all) global attention on
+2+ GPUs against the oracle.
 
 Each rank is a separate process on its own GPU (tests/_ring_worker.py); the
 concatenated shard outputs must match the oracle's single-sequence
@@ -33,11 +34,12 @@ def _gpus() -> int:
     return torch.cuda.device_count() if torch.cuda.is_available() else 0
 
 
-def _run_workers(tmp_path, world, T, H, dtype, seed, fused, unit, gen):
+def _run_workers(tmp_path, world, T, H, dtype, seed, fused, unit, gen, mode="ring"):
     port = _free_port()
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     procs = [subprocess.Popen([sys.executable, str(HERE / "_ring_worker.py"), str(r), str(world), str(port),
-                               str(tmp_path), str(T), str(H), dtype, str(seed), "1" if fused else "0", str(unit), gen],
+                               str(tmp_path), str(T), str(H), dtype, str(seed), "1" if fused else "0", str(unit), gen,
+                               mode],
                               env=env)
              for r in range(world)]
     rcs = [p.wait(timeout=900) for p in procs]
@@ -114,3 +116,49 @@ def test_ring_config4_length(tmp_path, world):
     rows = np.array(rows[:512], np.int64)
     ref = oracle.attention_rows(qn, kn, v, rows)
     oracle.gate(oracle.compare(out[rows], ref), 0.9999, 1e-2)
+
+
+# Head parallelism (hs_ring_ulysses_attention_fused): H must be a multiple of the ranks;
+# uneven token shards (1001 over 2 and 4) exercise the all-to-all's per-peer row counts.
+@pytest.mark.parametrize("world,T,H,fused,dtype", [
+    (2, 2748, 2, True, "bf16"), (2, 1001, 4, False, "f16"), (2, 2748, 6, True, "f16"),
+    (4, 5496, 4, True, "bf16"), (4, 1001, 8, False, "bf16"),
+    (8, 10992, 8, True, "bf16"), (8, 2003, 16, False, "f16"),
+])
+def test_ulysses_matches_oracle(tmp_path, world, T, H, fused, dtype):
+    if _gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
+    seed = 23
+    out = np.concatenate(_run_workers(tmp_path, world, T, H, dtype, seed, fused, 0, "np", "ulysses"), axis=2)
+    rng = np.random.default_rng(seed)
+    q, k, v = (oracle.round_to(dtype, rng.standard_normal((1, H, T, 64), np.float32)) for _ in range(3))
+    if fused:
+        q, k = _prep(q, k, dtype)
+    oracle.gate(oracle.compare(out, oracle.attention(q, k, v)), 0.9999, 1e-2)
+
+
+@pytest.mark.parametrize("world", [2, 8])
+def test_ulysses_config4_length(tmp_path, world):
+    """Config 4's length by head parallelism: 274,800 tokens, 16 heads, bf16, fused; 512 sampled
+    query rows over every head group against the oracle over all keys."""
+    if _gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch
+
+    from _ring_worker import device_inputs
+
+    T, H, dtype, seed = 200 * 1374, 16, "bf16", 3
+    out = np.concatenate(_run_workers(tmp_path, world, T, H, dtype, seed, True, 0, "torch", "ulysses"),
+                         axis=2).reshape(-1, 64)
+    q, k, v = (x.float().cpu().numpy() for x in device_inputs(torch.device("cuda", 0), T, H, dtype, seed))
+    qn, kn = _prep(q, k, dtype)
+    del q, k
+    rng = np.random.default_rng(2)
+    edges = set()
+    for r in range(world):
+        s0 = r * T // world
+        edges |= {max(0, min(T - 1, s0 + d)) for d in (-1, 0, 1)}
+    tokens = sorted(edges | {0, 5, 1374, T - 1} | set(int(x) for x in rng.integers(0, T, 24)))
+    rows = sorted({h * T + t for h in range(H) for t in tokens})
+    rows = np.array(rows[:512], np.int64)
+    oracle.gate(oracle.compare(out[rows], oracle.attention_rows(qn, kn, v, rows)), 0.9999, 1e-2)
