@@ -328,6 +328,11 @@ impl Drop for CudaTensor {
 }
 
 /// One rank of the multi-GPU ring (global attention over NCCL; one process per GPU).
+/// hs_ring_attention_fused and hs_ring_ulysses_attention_fused share one signature.
+type GlobalFn = unsafe extern "C" fn(*mut ffi::hs_ring, *const c_void, *const c_void, *const c_void, *mut c_void, u32,
+                                     u32, u32, ffi::hs_dtype, f32, *const f32, *const f32, *const f32, *const f32,
+                                     f32, *const f32, *const f32, u32, u32, u32) -> ffi::hs_status;
+
 pub struct Ring {
     raw: *mut ffi::hs_ring,
     ctx: Context,
@@ -358,9 +363,22 @@ impl Ring {
         check(unsafe { ffi::hs_ring_set_reserved_sms(self.raw, sms) })
     }
 
-    /// Global attention over this rank's shard (S = 1): q, k, v, out (H, T_r, 64).
+    /// Global attention over this rank's shard (S = 1): q, k, v, out (H, T_r, 64), by the K/V ring.
     pub fn attention_fused(&self, q: &CudaTensor, k: &CudaTensor, v: &CudaTensor, out: &CudaTensor, t_total: usize,
                            qk_norm: Option<&QkNorm<'_>>, rope: Option<&Rope<'_>>) -> Result<(), Error> {
+        self.global(ffi::hs_ring_attention_fused, q, k, v, out, t_total, qk_norm, rope)
+    }
+
+    /// The same contract by head parallelism: an all-to-all gathers the whole sequence of
+    /// H / world heads on each rank, one attention launch, an all-to-all back (H a multiple of world).
+    pub fn attention_ulysses(&self, q: &CudaTensor, k: &CudaTensor, v: &CudaTensor, out: &CudaTensor,
+                             t_total: usize, qk_norm: Option<&QkNorm<'_>>, rope: Option<&Rope<'_>>)
+                             -> Result<(), Error> {
+        self.global(ffi::hs_ring_ulysses_attention_fused, q, k, v, out, t_total, qk_norm, rope)
+    }
+
+    fn global(&self, call: GlobalFn, q: &CudaTensor, k: &CudaTensor, v: &CudaTensor, out: &CudaTensor,
+              t_total: usize, qk_norm: Option<&QkNorm<'_>>, rope: Option<&Rope<'_>>) -> Result<(), Error> {
         let h = q.shape[q.shape.len() - 3];
         let null = ptr::null::<f32>();
         let (qw, qb, kw, kb, eps) = match qk_norm {
@@ -373,9 +391,8 @@ impl Ring {
         };
         let _g = self.ctx.lock();
         check(unsafe {
-            ffi::hs_ring_attention_fused(self.raw, q.ptr, k.ptr, v.ptr, out.ptr, h as u32, t_total as u32, 64,
-                                         q.dtype.code(), 0.0, qw, qb, kw, kb, eps, sin, cos, rows as u32,
-                                         prefix as u32, tpf as u32)
+            call(self.raw, q.ptr, k.ptr, v.ptr, out.ptr, h as u32, t_total as u32, 64, q.dtype.code(), 0.0, qw, qb, kw,
+                 kb, eps, sin, cos, rows as u32, prefix as u32, tpf as u32)
         })
     }
 
