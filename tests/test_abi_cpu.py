@@ -38,6 +38,21 @@ def test_python_bindings_cover_the_header(L):
     assert set(_lib.header_symbols()) == bound
 
 
+def test_python_bindings_match_header_arity(L):
+    """Every ctypes binding passes as many arguments as the header's prototype declares."""
+    import re
+
+    text = re.sub(r"/\*.*?\*/", "", _lib.HEADER.read_text(), flags=re.S)
+    arity = {}
+    for name, params in re.findall(r"HS_API[^;(]*?\b(hs_[a-z0-9_]+)\s*\(([^)]*)\)\s*;", text, flags=re.S):
+        params = params.strip()
+        arity[name] = 0 if params in ("", "void") else params.count(",") + 1
+    bound = {**_lib.SIGNATURES, **session.RING_SIGNATURES}
+    assert set(bound) <= set(arity), sorted(set(bound) - set(arity))
+    wrong = {n: (len(args), arity[n]) for n, (_, args) in bound.items() if len(args) != arity[n]}
+    assert not wrong, f"(bound, declared) argument counts differ: {wrong}"
+
+
 def test_abi_version(L):
     assert L.hs_abi_version() == 2
 
